@@ -1,0 +1,386 @@
+#!/usr/bin/env python
+"""Benchmark of the BD3-LM attention hot path on B200 (one JSON line on rank 0).
+
+Headline workload: BD3-LM training attention forward + backward,
+B=8 per GPU, H=12, n=1024 per half (2n = 2048), head_dim 64, bf16, block_size 16, synthetic
+N(0,1) inputs from a seed. A step is one forward (O, LSE) and one backward (dQ, dK, dV)
+through the C ABI with the inputs resident in HBM; before every step a 256 MiB buffer is
+written to flush L2, outside the step's CUDA-event pair. The metric is useful TFLOP/s:
+forward 4*D*nnz*B*H FLOPs over the nnz = n^2 + n*bs visible (query, key) pairs, backward
+2.5x that (the reference's convention, bench/attention_bench.py:99).
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU (under torchrun): every rank runs the same per-GPU workload on its own batch
+shard (batch x head partition, no collective on the data path; weak scaling); the step
+time is the max over ranks. --impl reference times the reference's CPU path (the oracle
+restatement of model/modules.py:738-771 with autograd) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for _p in (REPO, os.path.join(REPO, "diffusion-llm_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+B, H, N_HALF, D, BS = 8, 12, 1024, 64, 16
+METRIC = "BD3-LM attn fwd+bwd TFLOP/s (useful FLOPs, bwd = 2.5x fwd)"
+UNIT = "TFLOP/s"
+
+
+def nnz(n: int, bs: int) -> int:
+    """Visible (query, key) pairs of block_diff_mask(n, bs) when bs divides n."""
+    return n * n + n * bs
+
+
+def useful_flops(b: int, n: int, bs: int) -> tuple[float, float]:
+    fwd = 4.0 * D * nnz(n, bs) * b * H
+    return fwd, 2.5 * fwd
+
+
+def load_peaks() -> dict:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        loaded = [s for s in sm if s >= 0.5 * max(sm)] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------
+def cpu_reference_step(n: int, bs: int, heads: int, gen_seed: int = 0) -> tuple[float, float]:
+    """One fwd+bwd of the reference's CPU attention (fp32, autograd) on a (1, heads, 2n, 64)
+    slice; returns (seconds, useful FLOPs of the slice)."""
+    import oracle
+    g = torch.Generator().manual_seed(gen_seed)
+    q, k, v, do = (torch.randn(1, heads, 2 * n, D, generator=g) for _ in range(4))
+    mask = torch.from_numpy(oracle.block_diff_mask(n, bs))
+    t0 = time.perf_counter()
+    oracle.attention_grads(q, k, v, do, mask, dtype=torch.float32)
+    dt = time.perf_counter() - t0
+    f, b = useful_flops(1, n, bs)
+    return dt, (f + b) * heads / H
+
+
+def cpu_baseline(reps: int = 3) -> dict:
+    torch.set_num_threads(os.cpu_count() or 1)
+    cpu_reference_step(N_HALF, BS, H)  # warm-up
+    times, flops = [], 0.0
+    for _ in range(reps):
+        dt, flops = cpu_reference_step(N_HALF, BS, H)
+        times.append(dt)
+    med = statistics.median(times)
+    return {"value": round(flops / med / 1e12, 6), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": f"fwd+bwd of a B=1 slice (12 heads, n={N_HALF}, bs={BS}) of the workload, "
+                      f"fp32, oracle restatement of model/modules.py:738-771 + autograd, "
+                      f"median of {reps} after 1 warm-up ({med:.2f} s each)"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_reference_step(N_HALF, BS, H)
+    total_t, total_f = 0.0, 0.0
+    for _ in range(args.steps):
+        dt, fl = cpu_reference_step(N_HALF, BS, H)
+        total_t += dt
+        total_f += fl
+    val = total_f / total_t / 1e12
+    sample = (f"each step: fwd+bwd of a B=1 slice (12 heads, n={N_HALF}, bs={BS}) of the "
+              f"B={B} workload, fp32 on the host cores (oracle restatement of "
+              f"model/modules.py:738-771 + autograd; the reference itself cannot travel)")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(val, 6), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_t / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"C2 fwd+bwd B={B} H={H} n={N_HALF} bs={BS} (B=1 slice per step)",
+                   "global_batch": B, "seq_len": 2 * N_HALF, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(val, 6), "unit": UNIT, "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(val, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ---------------------------------------------------------------------------------------
+def make_inputs(seed: int, dev):
+    g = torch.Generator().manual_seed(seed)
+    shape = (B, H, 2 * N_HALF, D)
+    return [torch.randn(shape, generator=g).to(torch.bfloat16).to(dev) for _ in range(4)]
+
+
+def time_steps(fn, steps: int, l2) -> list[float]:
+    """Per-step device times (ms) of fn(), each after an L2 flush outside its events."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for s, e in evs:
+        l2.zero_()
+        s.record()
+        fn()
+        e.record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
+    """Decode rows of BASELINE configs 3 and 4 (HBM-bound): time and achieved GB/s."""
+    out = {}
+    g = torch.Generator().manual_seed(5)
+    # C3: split-KV, B=32, H=12, q_len=16, cache 64K + the block itself
+    b3, kv3 = 32, 65536 + 16
+    q3 = torch.randn(b3, H, 16, D, generator=g).bfloat16().to(dev)
+    k3 = torch.empty(b3, H, kv3, D, dtype=torch.bfloat16, device=dev).normal_()
+    v3 = torch.empty_like(k3).normal_()
+    ms = time_steps(lambda: ops.decode_raw(q3, k3, v3, BS), reps, l2)
+    by = b3 * H * (256 * kv3 + 4096)
+    t = statistics.median(ms)
+    out["splitkv_b32_kv64k"] = {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
+                                "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
+    del k3, v3
+    # C4: live-block decode, B=16, kv 8192, 32 of 128 64-token blocks live per (b, h)
+    b4, kv4, nb, live = 16, 8192, 128, 32
+    q4 = torch.randn(b4, H, 16, D, generator=g).bfloat16().to(dev)
+    k4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
+    v4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
+    idx = torch.stack([torch.cat([torch.randperm(nb - 1, generator=g)[:live - 1].sort().values,
+                                  torch.tensor([nb - 1])]) for _ in range(b4 * H)])
+    idx = idx.view(b4, H, live).int().to(dev)
+    cnt = torch.full((b4, H), live, dtype=torch.int32, device=dev)
+    ms = time_steps(lambda: ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS), reps, l2)
+    by = b4 * H * (live * 64 * 256 + 4096)
+    t = statistics.median(ms)
+    out["live_b16_kv8k_25pct"] = {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
+                                  "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
+    return out
+
+
+def run_ours(args) -> None:
+    world, rank, local = dist_setup(args.gpus)
+    from bd3attn import ops
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+
+    dev = torch.device("cuda", local)
+    peaks = load_peaks()
+    q, k, v, do = make_inputs(1000 + rank, dev)
+    l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    fwd_f, bwd_f = useful_flops(B, N_HALF, BS)
+
+    def step():
+        o, lse = ops.attn_fwd_raw(q, k, v, BS)
+        ops.attn_bwd_raw(q, k, v, o, lse, do, BS)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier(world)
+    ops.profile_enable(True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        ms = time_steps(step, args.steps, l2)
+        barrier(world)
+    prof = ops.profile_collect()
+    ops.profile_enable(False)
+    total_ms = max_over_ranks(sum(ms), world)
+    value = (fwd_f + bwd_f) * args.steps * world / (total_ms * 1e-3) / 1e12
+
+    # roofline of the dominant kernel: algorithmic FLOPs per launch / its mean duration
+    per_launch_mm = {"attn_fwd": 2, "bwd_dq": 3, "bwd_dkdv": 4}  # nnz-restricted matmuls
+    dom = max((kname for kname in prof if kname in per_launch_mm), key=lambda kk: prof[kk][0])
+    dom_ms = prof[dom][0] / prof[dom][1]
+    algo = per_launch_mm[dom] * 2.0 * D * nnz(N_HALF, BS) * B * H
+    achieved = algo / (dom_ms * 1e-3) / 1e12
+    launches = sum(c for _, c in prof.values())
+
+    # bs = 4 (the other block size of config 2), same protocol, reported beside
+    def step4():
+        o, lse = ops.attn_fwd_raw(q, k, v, 4)
+        ops.attn_bwd_raw(q, k, v, o, lse, do, 4)
+    for _ in range(3):
+        step4()
+    ms4 = time_steps(step4, args.steps, l2)
+    f4, b4 = useful_flops(B, N_HALF, 4)
+    bs4 = (f4 + b4) / (statistics.mean(ms4) * 1e-3) / 1e12
+
+    # e2e: the public autograd API with host buffers, H2D + fwd + bwd + D2H every step
+    host = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+
+    def e2e_step():
+        qd, kd, vd, dod = (h.to(dev, non_blocking=True) for h in host)
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        o = BlockSparseFlashAttention.apply(qd, kd, vd, BS)
+        grads = torch.autograd.grad(o, (qd, kd, vd), dod)
+        for dst, src in zip(outs, grads):
+            dst.copy_(src, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier(world)
+    e2e_ms = max_over_ranks(sum(time_steps(e2e_step, args.steps, l2)), world)
+    e2e_val = (fwd_f + bwd_f) * args.steps * world / (e2e_ms * 1e-3) / 1e12
+    tensor_bytes = q.numel() * q.element_size()
+
+    extra = {"fwd_ms": round(prof["attn_fwd"][0] / prof["attn_fwd"][1], 4),
+             "kernels_ms_per_launch": {kk: round(t / c, 4) for kk, (t, c) in prof.items()},
+             "bs4_tflops": round(bs4, 2),
+             "dense_equiv_fwd_tflops_ref_convention": round(
+                 4.0 * B * H * (2 * N_HALF) ** 2 * D / (prof["attn_fwd"][0] / prof["attn_fwd"][1]
+                                                         * 1e-3) / 1e12, 2)}
+    if not args.no_decode:
+        extra["decode"] = decode_extras(ops, dev, l2, peaks)
+    cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1) from a seed",
+            "config": {"workload": f"C2: BD3-LM training attention fwd+bwd, B={B}/GPU, H={H}, "
+                                   f"n={N_HALF} (2n={2 * N_HALF}), D={D}, bs={BS}",
+                       "global_batch": B * world, "seq_len": 2 * N_HALF,
+                       "parallelism": f"batch x head shards over {world} GPU(s), no collective",
+                       "l2": "256 MiB buffer written before every step (outside the events)"},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 2),
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+                         "peak_source": peaks["source"] + " burst bf16"},
+            "e2e": {"value": round(e2e_val, 3), "unit": UNIT,
+                    "h2d_bytes_per_step": 4 * tensor_bytes, "d2h_bytes_per_step": 3 * tensor_bytes},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode extras")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

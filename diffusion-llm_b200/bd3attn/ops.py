@@ -1,0 +1,231 @@
+"""Tensor-level wrappers over the C ABI (one call per entry point of include/bd3_attn.h).
+
+Every function takes CUDA tensors, allocates its outputs (and workspace) with the caching
+allocator, and enqueues the kernels on the current CUDA stream of the inputs' device.
+They are also registered as ``torch.ops.bd3.*`` custom ops with fake (meta) implementations
+so that ``torch.compile`` can trace callers without graph breaks.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from bd3attn._lib import (BD3_BF16, BD3_F16, BD3_F32, LIB, check, i64_array)
+
+_DTYPE_CODE = {torch.bfloat16: BD3_BF16, torch.float16: BD3_F16, torch.float32: BD3_F32}
+
+
+def _code(dtype: torch.dtype) -> int:
+    if dtype not in _DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {dtype}")
+    return _DTYPE_CODE[dtype]
+
+
+def _rows_contig(x: torch.Tensor) -> torch.Tensor:
+    """The kernels read rows with TMA: the last dim must be contiguous and the other
+    strides 16-byte multiples; other layouts are copied (as the reference's
+    _last_stride_1 / .contiguous() do)."""
+    if x.stride(-1) != 1 or any((s * x.element_size()) % 16 for s in x.stride()[:-1]) \
+            or x.data_ptr() % 16:
+        return x.contiguous()
+    return x
+
+
+def _s3(x: torch.Tensor):
+    return (x.stride(0), x.stride(1), x.stride(2))
+
+
+def _stream(x: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+
+
+def _ptr(x):
+    return ctypes.c_void_p(x.data_ptr()) if x is not None else ctypes.c_void_p(0)
+
+
+def _check_cuda(*xs):
+    for x in xs:
+        if not x.is_cuda:
+            raise AssertionError("inputs must be on CUDA")
+
+
+# ---------------------------------------------------------------------------------------
+def attn_fwd_raw(q, k, v, block_size: int):
+    """(O, LSE) of BD3-LM training attention; q, k, v: (B, H, 2n, 64) bf16/f16."""
+    _check_cuda(q, k, v)
+    q, k, v = _rows_contig(q), _rows_contig(k), _rows_contig(v)
+    B, H, S, D = q.shape
+    o = torch.empty((B, H, S, D), dtype=q.dtype, device=q.device)
+    lse = torch.empty((B, H, S), dtype=torch.float32, device=q.device)
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o))
+    with torch.cuda.device(q.device):
+        check("bd3_attn_fwd", LIB.bd3_attn_fwd(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, S // 2, D, strides,
+            int(block_size), _code(q.dtype), _stream(q)))
+    return o, lse
+
+
+def attn_bwd_raw(q, k, v, o, lse, do, block_size: int):
+    """(dQ, dK, dV) of BD3-LM training attention."""
+    _check_cuda(q, k, v, o, lse, do)
+    q, k, v, o, do = (_rows_contig(t) for t in (q, k, v, o, do))
+    B, H, S, D = q.shape
+    dq = torch.empty((B, H, S, D), dtype=q.dtype, device=q.device)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    ws_bytes = LIB.bd3_attn_bwd_workspace_size(B, H, S // 2, D)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
+    lse = lse.contiguous()
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o) + _s3(do) + _s3(dq) + _s3(dk)
+                        + _s3(dv))
+    with torch.cuda.device(q.device):
+        check("bd3_attn_bwd", LIB.bd3_attn_bwd(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _ptr(do), _ptr(dq), _ptr(dk),
+            _ptr(dv), B, H, S // 2, D, strides, int(block_size), _code(q.dtype), _ptr(ws),
+            ws.numel(), _stream(q)))
+    return dq, dk, dv
+
+
+def decode_plan(B, H, q_len, kv_len, block_size, q_pos0=-1, kv_pos0=0):
+    ns = ctypes.c_int64(0)
+    wb = ctypes.c_size_t(0)
+    check("bd3_decode_plan", LIB.bd3_decode_plan(B, H, q_len, kv_len, block_size, q_pos0,
+                                                 kv_pos0, ctypes.byref(ns), ctypes.byref(wb)))
+    return ns.value, wb.value
+
+
+def decode_raw(q, k, v, block_size: int, q_pos0: int = -1, kv_pos0: int = 0,
+               out_dtype=None, return_lse: bool = False, n_splits: int | None = None):
+    """Block-causal decode attention of the q_len queries over kv_len keys."""
+    _check_cuda(q, k, v)
+    q, k, v = _rows_contig(q), _rows_contig(k), _rows_contig(v)
+    B, H, q_len, D = q.shape
+    kv_len = k.shape[2]
+    out_dtype = q.dtype if out_dtype is None else out_dtype
+    ns, wb = decode_plan(B, H, q_len, kv_len, int(block_size), q_pos0, kv_pos0)
+    if n_splits is not None and q_len <= 64:
+        ns = int(n_splits)
+        wb = B * H * ns * q_len * 65 * 4 if ns > 1 else 0
+    o = torch.empty((B, H, q_len, D), dtype=out_dtype, device=q.device)
+    lse = torch.empty((B, H, q_len), dtype=torch.float32, device=q.device) if return_lse else None
+    ws = torch.empty(max(wb, 16), dtype=torch.uint8, device=q.device)
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o))
+    with torch.cuda.device(q.device):
+        check("bd3_decode_attn", LIB.bd3_decode_attn(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, q_len, kv_len, D, strides,
+            int(block_size), int(q_pos0), int(kv_pos0), ns, _code(q.dtype), _code(out_dtype),
+            _ptr(ws), wb, _stream(q)))
+    return (o, lse) if return_lse else o
+
+
+def live_decode_raw(q, k, v, live_idx, live_cnt, kv_block: int, block_size: int,
+                    out_dtype=None, return_lse: bool = False):
+    """Decode over a per-(batch, head) list of live KV blocks.
+
+    live_idx: (B, H, max_live) int32 ascending block indices (entries past live_cnt ignored);
+    live_cnt: (B, H) int32.
+    """
+    _check_cuda(q, k, v, live_idx, live_cnt)
+    q, k, v = _rows_contig(q), _rows_contig(k), _rows_contig(v)
+    B, H, q_len, D = q.shape
+    kv_len = k.shape[2]
+    out_dtype = q.dtype if out_dtype is None else out_dtype
+    live_idx = live_idx.to(torch.int32).contiguous()
+    live_cnt = live_cnt.to(torch.int32).contiguous()
+    max_live = live_idx.shape[-1]
+    ns = ctypes.c_int64(0)
+    wb = ctypes.c_size_t(0)
+    check("bd3_decode_live_plan", LIB.bd3_decode_live_plan(
+        B, H, q_len, max_live, int(kv_block), ctypes.byref(ns), ctypes.byref(wb)))
+    o = torch.empty((B, H, q_len, D), dtype=out_dtype, device=q.device)
+    lse = torch.empty((B, H, q_len), dtype=torch.float32, device=q.device) if return_lse else None
+    ws = torch.empty(max(wb.value, 16), dtype=torch.uint8, device=q.device)
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o))
+    with torch.cuda.device(q.device):
+        check("bd3_decode_live_blocks", LIB.bd3_decode_live_blocks(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _ptr(live_idx), _ptr(live_cnt),
+            max_live, max_live, int(kv_block), B, H, q_len, kv_len, D, strides, int(block_size),
+            ns.value, _code(q.dtype), _code(out_dtype), _ptr(ws), wb.value, _stream(q)))
+    return (o, lse) if return_lse else o
+
+
+def lse_merge_raw(parts, lses, out_dtype=torch.bfloat16):
+    """Merge G partials: parts (G, B, H, rows, 64) fp32, lses (G, B, H, rows) fp32 ->
+    (O (B, H, rows, 64) in out_dtype, LSE (B, H, rows) fp32)."""
+    _check_cuda(parts, lses)
+    parts = parts.contiguous()
+    lses = lses.contiguous()
+    G, B, H, rows, D = parts.shape
+    o = torch.empty((B, H, rows, D), dtype=out_dtype, device=parts.device)
+    lse = torch.empty((B, H, rows), dtype=torch.float32, device=parts.device)
+    with torch.cuda.device(parts.device):
+        check("bd3_lse_merge", LIB.bd3_lse_merge(
+            _ptr(parts), _ptr(lses), _ptr(o), _ptr(lse), B, H, G, rows, D, B * H * rows * D,
+            rows * D, B * H * rows, rows, i64_array(_s3(o)), _code(out_dtype), _stream(parts)))
+    return o, lse
+
+
+def device_status(clear: bool = True) -> int:
+    """Sticky device-side error bits (1: a bounded wait ran out). Synchronises."""
+    return int(LIB.bd3_device_status(1 if clear else 0))
+
+
+# ---------------------------------------------------------------------------------------
+# torch.library registrations (used under torch.compile; eager callers use the raw calls)
+@torch.library.custom_op("bd3::attn_fwd", mutates_args=())
+def attn_fwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                block_size: int) -> tuple[torch.Tensor, torch.Tensor]:
+    return attn_fwd_raw(q, k, v, block_size)
+
+
+@attn_fwd_op.register_fake
+def _(q, k, v, block_size):
+    B, H, S, D = q.shape
+    return q.new_empty((B, H, S, D)), q.new_empty((B, H, S), dtype=torch.float32)
+
+
+@torch.library.custom_op("bd3::attn_bwd", mutates_args=())
+def attn_bwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
+                lse: torch.Tensor, do: torch.Tensor,
+                block_size: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return attn_bwd_raw(q, k, v, o, lse, do, block_size)
+
+
+@attn_bwd_op.register_fake
+def _(q, k, v, o, lse, do, block_size):
+    shape = tuple(q.shape)
+    return q.new_empty(shape), q.new_empty(shape), q.new_empty(shape)
+
+
+@torch.library.custom_op("bd3::decode", mutates_args=())
+def decode_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+              block_size: int) -> torch.Tensor:
+    return decode_raw(q, k, v, block_size)
+
+
+@decode_op.register_fake
+def _(q, k, v, block_size):
+    return q.new_empty(tuple(q.shape))
+
+
+# ---------------------------------------------------------------------------------------
+PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_delta", "bwd_dq", "bwd_dkdv", "decode",
+                   "decode_combine")
+
+
+def profile_enable(on: bool = True) -> None:
+    """Bracket every library launch with CUDA events on its own stream (see
+    bd3_profile_enable)."""
+    check("bd3_profile_enable", LIB.bd3_profile_enable(1 if on else 0))
+
+
+def profile_collect() -> dict:
+    """{kernel name: (total ms, launches)} for the launches since the last collect."""
+    ms = (ctypes.c_double * 8)()
+    cnt = (ctypes.c_int32 * 8)()
+    n = LIB.bd3_profile_collect(ms, cnt)
+    if n < 0:
+        check("bd3_profile_collect", -n)
+    return {PROFILE_KERNELS[i]: (ms[i], cnt[i]) for i in range(len(PROFILE_KERNELS)) if cnt[i]}

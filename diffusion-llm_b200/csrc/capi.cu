@@ -1,0 +1,659 @@
+// C-ABI entry points of libbd3attn.so (declared in include/bd3_attn.h).
+//
+// Host side only: argument validation (mirroring the reference's assertions), TMA tensor
+// map construction, launch planning and kernel launches. No allocation happens here: the
+// caller passes every output and workspace buffer.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/bd3_attn.h"
+#include "attn_bwd.cuh"
+#include "attn_fwd.cuh"
+#include "decode.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(BD3_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ---- cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda) ----
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+size_t elem_bytes(int dtype) { return dtype == BD3_F32 ? 4 : 2; }
+
+// 4-D map over (head_dim=64, seq, heads, batch) with a {64, box_rows, 1, 1} box, 128-byte
+// swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* map, const void* ptr, int dtype, int64_t seq, int64_t H, int64_t B,
+             const int64_t* strides /* b, h, s */, int box_rows, const char* name) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(BD3_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const size_t es = elem_bytes(dtype);
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0)
+    return fail(BD3_ERR_INVALID, "%s: pointer must be 16-byte aligned", name);
+  cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(seq), static_cast<cuuint64_t>(H),
+                        static_cast<cuuint64_t>(B)};
+  int64_t sb = strides[0], sh = strides[1], ss = strides[2];
+  // a size-1 dimension is never stepped over: give it a legal stride
+  if (seq == 1) ss = 64;
+  if (H == 1) sh = ss * seq;
+  if (B == 1) sb = sh * H;
+  const int64_t st[3] = {ss, sh, sb};
+  cuuint64_t gstr[3];
+  for (int i = 0; i < 3; ++i) {
+    const int64_t bytes = st[i] * static_cast<int64_t>(es);
+    if (st[i] <= 0 || bytes % 16 != 0 || bytes >= (int64_t(1) << 40))
+      return fail(BD3_ERR_INVALID,
+                  "%s: strides must be positive multiples of 16 bytes (got %lld elements)", name,
+                  static_cast<long long>(st[i]));
+    gstr[i] = static_cast<cuuint64_t>(bytes);
+  }
+  cuuint32_t box[4] = {64, static_cast<cuuint32_t>(box_rows), 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == BD3_BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : dtype == BD3_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                    : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const CUresult r = fn(map, dt, 4, const_cast<void*>(ptr), dims, gstr, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BD3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", name, int(r));
+  return BD3_OK;
+}
+
+int current_device_sms(int* sms) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  static int cache[64] = {0};
+  if (dev < 64 && cache[dev] > 0) {
+    *sms = cache[dev];
+    return BD3_OK;
+  }
+  e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+  if (dev < 64) cache[dev] = *sms;
+  return BD3_OK;
+}
+
+// Opt a kernel into its dynamic shared memory once per device.
+template <typename K>
+int set_smem(K kernel, uint32_t bytes, int slot) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  static bool done[64][32] = {};
+  if (dev < 64 && slot < 32 && done[dev][slot]) return BD3_OK;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  if (dev < 64 && slot < 32) done[dev][slot] = true;
+  return BD3_OK;
+}
+
+
+// ---- optional per-kernel timing (bd3_profile_*): CUDA event pairs around each launch ----
+enum ProfId { kPfFwd = 0, kPfPrefill, kPfDelta, kPfDq, kPfDkdv, kPfDecode, kPfCombine, kPfNum };
+constexpr int kProfCap = 8192;
+struct Prof {
+  bool on = false;
+  int n = 0;
+  int id[kProfCap];
+  cudaEvent_t ev[kProfCap][2];
+  bool created = false;
+};
+Prof& prof() {
+  static Prof p;
+  return p;
+}
+struct ProfScope {
+  int slot = -1;
+  cudaStream_t st;
+  ProfScope(int kernel, cudaStream_t s) : st(s) {
+    Prof& p = prof();
+    if (!p.on || p.n >= kProfCap) return;
+    slot = p.n++;
+    p.id[slot] = kernel;
+    cudaEventRecord(p.ev[slot][0], st);
+  }
+  ~ProfScope() {
+    if (slot >= 0) cudaEventRecord(prof().ev[slot][1], st);
+  }
+};
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? BD3_OK : cuda_fail(e, what);
+}
+
+int check_dims(int64_t B, int64_t H, int64_t D, int dtype) {
+  if (B < 1 || H < 1) return fail(BD3_ERR_INVALID, "batch and heads must be >= 1");
+  if (D != 64) return fail(BD3_ERR_UNSUPPORTED, "head_dim must be 64 (got %lld)", (long long)D);
+  if (dtype != BD3_BF16 && dtype != BD3_F16)
+    return fail(BD3_ERR_UNSUPPORTED, "inputs must be bf16 or f16 (dtype code %d)", dtype);
+  if (B * H > 65535 * 1024LL) return fail(BD3_ERR_UNSUPPORTED, "batch * heads too large");
+  return BD3_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, float* lse,
+               int64_t B, int64_t H, int64_t n, int64_t q_len, int64_t kv_len,
+               const int64_t* strides, int64_t bs, int dtype, cudaStream_t stream) {
+  CUtensorMap tq, tk, tv;
+  const int64_t q_rows = mode == bd3::kTrain ? 2 * n : q_len;
+  const int64_t kv_rows = mode == bd3::kTrain ? 2 * n : kv_len;
+  int rc;
+  if ((rc = make_map(&tq, q, dtype, q_rows, H, B, strides + 0, bd3::kFwdBM, "q")) != BD3_OK) return rc;
+  if ((rc = make_map(&tk, k, dtype, kv_rows, H, B, strides + 3, bd3::kFwdBN, "k")) != BD3_OK) return rc;
+  if ((rc = make_map(&tv, v, dtype, kv_rows, H, B, strides + 6, bd3::kFwdBN, "v")) != BD3_OK) return rc;
+  const int64_t* so = strides + 9;
+  if (reinterpret_cast<uintptr_t>(o) % 16 || so[0] % 8 || so[1] % 8 || so[2] % 8)
+    return fail(BD3_ERR_INVALID, "o: pointer and strides must be 16-byte aligned");
+  bd3::FwdParams p{};
+  p.o = o;
+  p.lse = lse;
+  p.o_sb = so[0];
+  p.o_sh = so[1];
+  p.o_ss = so[2];
+  p.lse_sh = q_rows;
+  p.lse_sb = H * q_rows;
+  p.H = static_cast<int>(H);
+  p.n = static_cast<int>(n);
+  p.q_len = static_cast<int>(q_len);
+  p.kv_len = static_cast<int>(kv_len);
+  p.bs = static_cast<int>(bs);
+  p.num_q_tiles = static_cast<int>(bd3::cdiv(static_cast<int>(q_rows), bd3::kFwdBM));
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  const int64_t grid = B * H * p.num_q_tiles;
+  if (grid > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "grid too large");
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const bd3::FwdParams);
+  int slot;
+  if (mode == bd3::kTrain) {
+    kern = dtype == BD3_BF16 ? bd3::attn_fwd_kernel<bd3::kTrain, true>
+                             : bd3::attn_fwd_kernel<bd3::kTrain, false>;
+    slot = dtype == BD3_BF16 ? 0 : 1;
+  } else {
+    kern = dtype == BD3_BF16 ? bd3::attn_fwd_kernel<bd3::kDecode, true>
+                             : bd3::attn_fwd_kernel<bd3::kDecode, false>;
+    slot = dtype == BD3_BF16 ? 2 : 3;
+  }
+  if ((rc = set_smem(kern, bd3::FwdSmem::kAlloc, slot)) != BD3_OK) return rc;
+  ProfScope ps(mode == bd3::kTrain ? kPfFwd : kPfPrefill, stream);
+  kern<<<static_cast<unsigned>(grid), bd3::kFwdThreads, bd3::FwdSmem::kAlloc, stream>>>(tq, tk, tv, p);
+  return check_launch("attn_fwd_kernel launch");
+}
+
+// Visible-key bound of the last query row: tiles at or past it are never read.
+int64_t decode_hi(int64_t q_len, int64_t kv_len, int64_t bs, int64_t q_pos0, int64_t kv_pos0) {
+  const int64_t hi = ((q_pos0 + q_len - 1) / bs + 1) * bs - kv_pos0;
+  return hi < kv_len ? hi : kv_len;
+}
+
+// Pick units (key tiles or live entries) per split with a small cost model: whole waves of
+// resident CTAs times (units per CTA + a fixed per-CTA overhead of 1.5 units).
+int64_t pick_units_per_split(int64_t ctas_per_split_unit_group, int64_t units, int sms) {
+  const int64_t slots = static_cast<int64_t>(sms) * 3;  // 3 resident decode CTAs per SM
+  int64_t best_u = 1;
+  double best = 1e300;
+  for (int64_t u = 1; u <= 64 && u <= units; ++u) {
+    const int64_t ctas = ctas_per_split_unit_group * ((units + u - 1) / u);
+    const double est = static_cast<double>((ctas + slots - 1) / slots) * (u + 1.5);
+    if (est <= best) {
+      best = est;
+      best_u = u;
+    }
+  }
+  return best_u;
+}
+
+}  // namespace
+
+extern "C" {
+
+int bd3_version(void) { return 100; }
+
+const char* bd3_last_error(void) { return g_last_error.c_str(); }
+
+int bd3_device_status(int clear) {
+  unsigned v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, bd3::g_bd3_status, sizeof(v));
+  if (e != cudaSuccess) {
+    cuda_fail(e, "reading the device status");
+    return -1;
+  }
+  if (clear && v) {
+    unsigned z = 0;
+    e = cudaMemcpyToSymbol(bd3::g_bd3_status, &z, sizeof(z));
+    if (e != cudaSuccess) {
+      cuda_fail(e, "clearing the device status");
+      return -1;
+    }
+  }
+  return static_cast<int>(v);
+}
+
+int bd3_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
+                 int64_t H, int64_t n, int64_t D, const int64_t* strides, int64_t block_size,
+                 int dtype, void* stream) {
+  int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  if (n < 1 || n % bd3::kFwdBM != 0)
+    return fail(BD3_ERR_INVALID, "n must be a positive multiple of 128 (got %lld)", (long long)n);
+  if (n > (1 << 29)) return fail(BD3_ERR_UNSUPPORTED, "sequence too long");
+  if (block_size < 1) return fail(BD3_ERR_INVALID, "block_size must be >= 1");
+  if (lse == nullptr || reinterpret_cast<uintptr_t>(lse) % 4)
+    return fail(BD3_ERR_INVALID, "lse must be a valid fp32 buffer");
+  return launch_fwd(bd3::kTrain, q, k, v, o, lse, B, H, n, 2 * n, 2 * n, strides, block_size,
+                    dtype, static_cast<cudaStream_t>(stream));
+}
+
+size_t bd3_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D) {
+  (void)D;
+  if (B < 1 || H < 1 || n < 1) return 0;
+  return static_cast<size_t>(B * H * 2 * n) * sizeof(float);
+}
+
+int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                 const void* dout, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                 int64_t n, int64_t D, const int64_t* strides, int64_t block_size, int dtype,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  if (n < 1 || n % bd3::kBwdBKV != 0)
+    return fail(BD3_ERR_INVALID, "n must be a positive multiple of 128 (got %lld)", (long long)n);
+  if (n > (1 << 29)) return fail(BD3_ERR_UNSUPPORTED, "sequence too long");
+  if (block_size < 1 || n % block_size != 0)
+    return fail(BD3_ERR_INVALID, "n must be a multiple of block_size (n=%lld, block_size=%lld)",
+                (long long)n, (long long)block_size);
+  const size_t need = bd3_attn_bwd_workspace_size(B, H, n, D);
+  if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 16)
+    return fail(BD3_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,
+                workspace_bytes);
+  if (lse == nullptr) return fail(BD3_ERR_INVALID, "lse is required");
+  const int64_t S = 2 * n;
+  CUtensorMap tq, tk, tv, tdo;
+  if ((rc = make_map(&tq, q, dtype, S, H, B, strides + 0, 128, "q")) != BD3_OK) return rc;
+  if ((rc = make_map(&tk, k, dtype, S, H, B, strides + 3, 128, "k")) != BD3_OK) return rc;
+  if ((rc = make_map(&tv, v, dtype, S, H, B, strides + 6, 128, "v")) != BD3_OK) return rc;
+  if ((rc = make_map(&tdo, dout, dtype, S, H, B, strides + 12, 128, "dout")) != BD3_OK) return rc;
+  const void* ptrs[5] = {o, dout, dq, dk, dv};
+  const int idx[5] = {9, 12, 15, 18, 21};
+  const char* names[5] = {"o", "dout", "dq", "dk", "dv"};
+  for (int t = 0; t < 5; ++t) {
+    const int64_t* s3 = strides + idx[t];
+    if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 || s3[0] % 8 || s3[1] % 8 || s3[2] % 8)
+      return fail(BD3_ERR_INVALID, "%s: pointer and strides must be 16-byte aligned", names[t]);
+  }
+  bd3::BwdParams p{};
+  p.o = o;
+  p.dout = dout;
+  p.lse = lse;
+  p.delta = static_cast<float*>(workspace);
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.o_sb = strides[9]; p.o_sh = strides[10]; p.o_ss = strides[11];
+  p.do_sb = strides[12]; p.do_sh = strides[13]; p.do_ss = strides[14];
+  p.dq_sb = strides[15]; p.dq_sh = strides[16]; p.dq_ss = strides[17];
+  p.dk_sb = strides[18]; p.dk_sh = strides[19]; p.dk_ss = strides[20];
+  p.dv_sb = strides[21]; p.dv_sh = strides[22]; p.dv_ss = strides[23];
+  p.H = static_cast<int>(H);
+  p.n = static_cast<int>(n);
+  p.bs = static_cast<int>(block_size);
+  p.num_tiles = static_cast<int>(S / 128);
+  p.scale = 0.125f;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf = dtype == BD3_BF16;
+  const int64_t rows = B * H * S;
+  const unsigned dblocks = static_cast<unsigned>((rows * 8 + 255) / 256);
+  {
+    ProfScope ps(kPfDelta, st);
+    if (bf) bd3::bwd_delta_kernel<true><<<dblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    else bd3::bwd_delta_kernel<false><<<dblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+  }
+  if ((rc = check_launch("bwd_delta_kernel launch")) != BD3_OK) return rc;
+  const unsigned grid = static_cast<unsigned>(B * H * p.num_tiles);
+  auto dqk = bf ? bd3::bwd_dq_kernel<true> : bd3::bwd_dq_kernel<false>;
+  if ((rc = set_smem(dqk, bd3::DqSmem::kAlloc, 4 + (bf ? 0 : 1))) != BD3_OK) return rc;
+  {
+    ProfScope ps(kPfDq, st);
+    dqk<<<grid, bd3::kBwdThreads, bd3::DqSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
+  }
+  if ((rc = check_launch("bwd_dq_kernel launch")) != BD3_OK) return rc;
+  auto dkv = bf ? bd3::bwd_dkdv_kernel<true> : bd3::bwd_dkdv_kernel<false>;
+  if ((rc = set_smem(dkv, bd3::DkdvSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
+  {
+    ProfScope ps(kPfDkdv, st);
+    dkv<<<grid, bd3::kBwdThreads, bd3::DkdvSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
+  }
+  return check_launch("bwd_dkdv_kernel launch");
+}
+
+int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t block_size,
+                    int64_t q_pos0, int64_t kv_pos0, int64_t* n_splits, size_t* workspace_bytes) {
+  if (B < 1 || H < 1 || q_len < 1 || kv_len < 1 || block_size < 1)
+    return fail(BD3_ERR_INVALID, "decode sizes must be >= 1");
+  if (q_pos0 < 0) q_pos0 = kv_len - q_len;
+  if (q_len > 64) {  // prefill: the tcgen05 kernel, no splits
+    *n_splits = 1;
+    *workspace_bytes = 0;
+    return BD3_OK;
+  }
+  int sms = 148;
+  int rc = current_device_sms(&sms);
+  if (rc != BD3_OK) return rc;
+  const int64_t hi = decode_hi(q_len, kv_len, block_size, q_pos0, kv_pos0);
+  const int64_t tiles = hi > 0 ? (hi + bd3::kDecBN - 1) / bd3::kDecBN : 1;
+  const int64_t groups = (q_len + 31) / 32;
+  const int64_t u = pick_units_per_split(B * H * groups, tiles, sms);
+  const int64_t s = (tiles + u - 1) / u;
+  *n_splits = s;
+  *workspace_bytes = s > 1 ? static_cast<size_t>(B * H * s * q_len) * (64 + 1) * 4 : 0;
+  return BD3_OK;
+}
+
+namespace {
+int launch_decode(bool live, const void* q, const void* k, const void* v, void* o,
+                  float* lse_out, const int32_t* live_idx, const int32_t* live_cnt,
+                  int64_t live_stride, int64_t max_live, int64_t kv_block, int64_t B, int64_t H,
+                  int64_t q_len, int64_t kv_len, const int64_t* strides, int64_t bs,
+                  int64_t q_pos0, int64_t kv_pos0, int64_t n_splits, int dtype, int out_dtype,
+                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  const int kmb = q_len <= 16 ? 1 : 2;
+  const int64_t groups = q_len <= 32 ? 1 : (q_len + 31) / 32;
+  int rc;
+  CUtensorMap tq, tk, tv;
+  if ((rc = make_map(&tq, q, dtype, q_len, H, B, strides + 0, kmb * 16, "q")) != BD3_OK) return rc;
+  if ((rc = make_map(&tk, k, dtype, kv_len, H, B, strides + 3, bd3::kDecBN, "k")) != BD3_OK) return rc;
+  if ((rc = make_map(&tv, v, dtype, kv_len, H, B, strides + 6, bd3::kDecBN, "v")) != BD3_OK) return rc;
+  const int64_t* so = strides + 9;
+  const int64_t oal = out_dtype == BD3_F32 ? 4 : 8;
+  if (reinterpret_cast<uintptr_t>(o) % 16 || so[0] % oal || so[1] % oal || so[2] % oal)
+    return fail(BD3_ERR_INVALID, "o: pointer and strides must be 16-byte aligned");
+  if (n_splits < 1 || n_splits > 65535) return fail(BD3_ERR_INVALID, "n_splits out of range");
+  const size_t need = n_splits > 1 ? static_cast<size_t>(B * H * n_splits * q_len) * 65 * 4 : 0;
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need))
+    return fail(BD3_ERR_WORKSPACE, "decode workspace too small: need %zu bytes, got %zu", need,
+                workspace_bytes);
+  bd3::DecParams p{};
+  p.o = o;
+  p.lse = lse_out;
+  p.ws_o = static_cast<float*>(workspace);
+  p.ws_lse = need > 0 ? p.ws_o + B * H * n_splits * q_len * 64 : nullptr;
+  p.live_idx = live_idx;
+  p.live_cnt = live_cnt;
+  p.o_sb = so[0];
+  p.o_sh = so[1];
+  p.o_ss = so[2];
+  p.H = static_cast<int>(H);
+  p.q_len = static_cast<int>(q_len);
+  p.kv_len = static_cast<int>(kv_len);
+  p.bs = static_cast<int>(bs);
+  p.q_pos0 = static_cast<int>(q_pos0);
+  p.kv_pos0 = static_cast<int>(kv_pos0);
+  p.n_splits = static_cast<int>(n_splits);
+  if (live) {
+    p.tiles_per_split = static_cast<int>((max_live + n_splits - 1) / n_splits);
+  } else {
+    const int64_t hi = decode_hi(q_len, kv_len, bs, q_pos0, kv_pos0);
+    const int64_t tiles = hi > 0 ? (hi + bd3::kDecBN - 1) / bd3::kDecBN : 0;
+    p.tiles_per_split = static_cast<int>((tiles + n_splits - 1) / n_splits);
+    if (p.tiles_per_split < 1) p.tiles_per_split = 1;
+  }
+  p.live_stride = static_cast<int>(live_stride);
+  p.kv_block = static_cast<int>(kv_block);
+  p.out_f32 = out_dtype == BD3_F32 ? 1 : 0;
+  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  const dim3 grid(static_cast<unsigned>(n_splits), static_cast<unsigned>(B * H),
+                  static_cast<unsigned>(groups));
+  using Kern = void (*)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const bd3::DecParams);
+  Kern kern;
+  const bool bf = dtype == BD3_BF16;
+  if (live) {
+    kern = kmb == 1 ? (bf ? bd3::decode_kernel<1, true, true> : bd3::decode_kernel<1, false, true>)
+                    : (bf ? bd3::decode_kernel<2, true, true> : bd3::decode_kernel<2, false, true>);
+  } else {
+    kern = kmb == 1 ? (bf ? bd3::decode_kernel<1, true, false> : bd3::decode_kernel<1, false, false>)
+                    : (bf ? bd3::decode_kernel<2, true, false> : bd3::decode_kernel<2, false, false>);
+  }
+  const int slot = 8 + (live ? 4 : 0) + (kmb == 1 ? 0 : 2) + (bf ? 0 : 1);
+  if ((rc = set_smem(kern, bd3::DecSmem::kAlloc, slot)) != BD3_OK) return rc;
+  {
+    ProfScope ps(kPfDecode, stream);
+    kern<<<grid, bd3::kDecThreads, bd3::DecSmem::kAlloc, stream>>>(tq, tk, tv, p);
+  }
+  if ((rc = check_launch("decode_kernel launch")) != BD3_OK) return rc;
+  if (n_splits > 1) {
+    bd3::CombineParams c{};
+    c.parts = p.ws_o;
+    c.lses = p.ws_lse;
+    c.o = o;
+    c.lse_out = lse_out;
+    c.part_bh = n_splits * q_len * 64;
+    c.part_g = q_len * 64;
+    c.lse_bh = n_splits * q_len;
+    c.lse_g = q_len;
+    c.o_sb = so[0];
+    c.o_sh = so[1];
+    c.o_ss = so[2];
+    c.H = static_cast<int>(H);
+    c.G = static_cast<int>(n_splits);
+    c.rows = static_cast<int>(q_len);
+    c.n_bh = static_cast<int>(B * H);
+    c.out_dtype = out_dtype;
+    const int64_t threads = B * H * q_len * 8;
+    ProfScope ps(kPfCombine, stream);
+    bd3::decode_combine_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(c);
+    if ((rc = check_launch("decode_combine_kernel launch")) != BD3_OK) return rc;
+  }
+  return BD3_OK;
+}
+}  // namespace
+
+int bd3_decode_attn(const void* q, const void* k, const void* v, void* o, float* lse_out,
+                    int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t D,
+                    const int64_t* strides, int64_t block_size, int64_t q_pos0, int64_t kv_pos0,
+                    int64_t n_splits, int dtype, int out_dtype, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  if (q_len < 1 || kv_len < 1) return fail(BD3_ERR_INVALID, "q_len and kv_len must be >= 1");
+  if (q_len > kv_len && q_pos0 < 0)
+    return fail(BD3_ERR_INVALID, "queries are the last q_len key positions: q_len <= kv_len");
+  if (block_size < 1) return fail(BD3_ERR_INVALID, "block_size must be >= 1");
+  if (kv_len > (1LL << 30) || q_len > (1LL << 30)) return fail(BD3_ERR_UNSUPPORTED, "too long");
+  if (out_dtype != dtype && out_dtype != BD3_F32)
+    return fail(BD3_ERR_INVALID, "out_dtype must equal dtype or be fp32");
+  if (q_pos0 < 0) q_pos0 = kv_len - q_len;
+  if (kv_pos0 < 0) return fail(BD3_ERR_INVALID, "kv_pos0 must be >= 0");
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (q_len > 64) {
+    if (n_splits != 1 || q_pos0 != kv_len - q_len || kv_pos0 != 0 || out_dtype != dtype)
+      return fail(BD3_ERR_UNSUPPORTED,
+                  "prefill (q_len > 64) supports the reference placement and dtype only");
+    if (lse_out != nullptr) return fail(BD3_ERR_UNSUPPORTED, "prefill does not return LSE");
+    return launch_fwd(bd3::kDecode, q, k, v, o, nullptr, B, H, 0, q_len, kv_len, strides,
+                      block_size, dtype, st);
+  }
+  return launch_decode(false, q, k, v, o, lse_out, nullptr, nullptr, 0, 0, 64, B, H, q_len,
+                       kv_len, strides, block_size, q_pos0, kv_pos0, n_splits, dtype,
+                       out_dtype, workspace, workspace_bytes, st);
+}
+
+int bd3_decode_live_plan(int64_t B, int64_t H, int64_t q_len, int64_t max_live,
+                         int64_t kv_block, int64_t* n_splits, size_t* workspace_bytes) {
+  if (B < 1 || H < 1 || q_len < 1 || q_len > 64 || max_live < 1)
+    return fail(BD3_ERR_INVALID, "live decode: sizes must be >= 1 and q_len <= 64");
+  if (kv_block < 64 || kv_block % 64) return fail(BD3_ERR_UNSUPPORTED, "kv_block must be a multiple of 64");
+  int sms = 148;
+  int rc = current_device_sms(&sms);
+  if (rc != BD3_OK) return rc;
+  const int64_t groups = (q_len + 31) / 32;
+  const int64_t per = kv_block / 64;
+  // units are live entries; each entry is `per` tiles
+  int64_t u = pick_units_per_split(B * H * groups, max_live * per, sms);
+  u = (u + per - 1) / per;
+  const int64_t s = (max_live + u - 1) / u;
+  *n_splits = s;
+  *workspace_bytes = s > 1 ? static_cast<size_t>(B * H * s * q_len) * 65 * 4 : 0;
+  return BD3_OK;
+}
+
+int bd3_decode_live_blocks(const void* q, const void* k, const void* v, void* o,
+                           float* lse_out, const int32_t* live_idx, const int32_t* live_cnt,
+                           int64_t live_stride, int64_t max_live, int64_t kv_block, int64_t B,
+                           int64_t H, int64_t q_len, int64_t kv_len, int64_t D,
+                           const int64_t* strides, int64_t block_size, int64_t n_splits,
+                           int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  if (q_len < 1 || q_len > 64 || q_len > kv_len)
+    return fail(BD3_ERR_INVALID, "live decode needs 1 <= q_len <= min(64, kv_len)");
+  if (kv_block < 64 || kv_block % 64) return fail(BD3_ERR_UNSUPPORTED, "kv_block must be a multiple of 64");
+  if (live_idx == nullptr || live_cnt == nullptr || max_live < 1 || live_stride < max_live)
+    return fail(BD3_ERR_INVALID, "live block list missing or malformed");
+  if (block_size < 1) return fail(BD3_ERR_INVALID, "block_size must be >= 1");
+  if (out_dtype != dtype && out_dtype != BD3_F32)
+    return fail(BD3_ERR_INVALID, "out_dtype must equal dtype or be fp32");
+  return launch_decode(true, q, k, v, o, lse_out, live_idx, live_cnt, live_stride, max_live,
+                       kv_block, B, H, q_len, kv_len, strides, block_size, kv_len - q_len, 0,
+                       n_splits, dtype, out_dtype, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out, int64_t B,
+                  int64_t H, int64_t G, int64_t rows, int64_t D, const int64_t part_g,
+                  int64_t part_bh, int64_t lse_g, int64_t lse_bh, const int64_t* o_strides,
+                  int out_dtype, void* stream) {
+  if (B < 1 || H < 1 || G < 1 || rows < 1) return fail(BD3_ERR_INVALID, "merge sizes must be >= 1");
+  if (D != 64) return fail(BD3_ERR_UNSUPPORTED, "head_dim must be 64");
+  if (out_dtype < BD3_BF16 || out_dtype > BD3_F32) return fail(BD3_ERR_INVALID, "bad out_dtype");
+  if (reinterpret_cast<uintptr_t>(parts) % 16 || part_g % 4 || part_bh % 4)
+    return fail(BD3_ERR_INVALID, "parts must be 16-byte aligned");
+  const int64_t oal = out_dtype == BD3_F32 ? 4 : 8;
+  if (reinterpret_cast<uintptr_t>(o) % 16 || o_strides[0] % oal || o_strides[1] % oal ||
+      o_strides[2] % oal)
+    return fail(BD3_ERR_INVALID, "o: pointer and strides must be 16-byte aligned");
+  bd3::CombineParams c{};
+  c.parts = parts;
+  c.lses = lses;
+  c.o = o;
+  c.lse_out = lse_out;
+  c.part_g = part_g;
+  c.part_bh = part_bh;
+  c.lse_g = lse_g;
+  c.lse_bh = lse_bh;
+  c.o_sb = o_strides[0];
+  c.o_sh = o_strides[1];
+  c.o_ss = o_strides[2];
+  c.H = static_cast<int>(H);
+  c.G = static_cast<int>(G);
+  c.rows = static_cast<int>(rows);
+  c.n_bh = static_cast<int>(B * H);
+  c.out_dtype = out_dtype;
+  const int64_t threads = B * H * rows * 8;
+  bd3::decode_combine_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
+                               static_cast<cudaStream_t>(stream)>>>(c);
+  return check_launch("decode_combine_kernel launch");
+}
+
+
+int bd3_profile_enable(int on) {
+  Prof& p = prof();
+  if (on && !p.created) {
+    for (int i = 0; i < kProfCap; ++i)
+      for (int j = 0; j < 2; ++j) {
+        const cudaError_t e = cudaEventCreate(&p.ev[i][j]);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+      }
+    p.created = true;
+  }
+  p.on = on != 0;
+  p.n = 0;
+  return BD3_OK;
+}
+
+int bd3_profile_collect(double* total_ms, int32_t* counts) {
+  Prof& p = prof();
+  for (int k = 0; k < kPfNum; ++k) {
+    total_ms[k] = 0.0;
+    counts[k] = 0;
+  }
+  for (int i = 0; i < p.n; ++i) {
+    cudaError_t e = cudaEventSynchronize(p.ev[i][1]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, p.ev[i][0], p.ev[i][1]);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime");
+    total_ms[p.id[i]] += ms;
+    counts[p.id[i]] += 1;
+  }
+  p.n = 0;
+  return kPfNum;
+}
+
+int bd3_debug_ranges(int kind, int64_t start, int64_t tile_a, int64_t tile_b, int64_t n_or_qlen,
+                     int64_t kv_len, int64_t block_size, int32_t* out) {
+  bd3::Range r[4];
+  int cnt = 0;
+  const int s = static_cast<int>(start), a = static_cast<int>(tile_a),
+            b = static_cast<int>(tile_b), nq = static_cast<int>(n_or_qlen),
+            kv = static_cast<int>(kv_len), bs = static_cast<int>(block_size);
+  if (kind == 0) cnt = bd3::fwd_ranges(s, a, b, nq, bs, r);
+  else if (kind == 1) cnt = bd3::dkdv_ranges(s, a, b, nq, bs, r);
+  else if (kind == 2) cnt = bd3::decode_ranges(s, a, b, nq, kv, bs, r);
+  else return fail(BD3_ERR_INVALID, "unknown range kind %d", kind);
+  for (int i = 0; i < cnt; ++i) {
+    out[4 * i + 0] = r[i].lo;
+    out[4 * i + 1] = r[i].hi;
+    out[4 * i + 2] = r[i].rule;
+    out[4 * i + 3] = r[i].shift;
+  }
+  return cnt;
+}
+
+int bd3_debug_tiles(int32_t* out) {
+  out[0] = bd3::kFwdBM;
+  out[1] = bd3::kFwdBN;
+  out[2] = bd3::kBwdBKV;
+  out[3] = bd3::kBwdBQ;
+  out[4] = bd3::kDecBN;
+  out[5] = bd3::kBwdDqBM;
+  return 6;
+}
+
+}  // extern "C"

@@ -1,0 +1,41 @@
+"""Split-KV (FlashDecoding) attention for BD3-LM cached sampling, on B200.
+
+Drop-in for kernels/SplitKVDecodeAttention.py of the reference:
+``split_kv_decode_attention(q, k, v, block_size)`` (:130-171), same result as
+block_sparse_decode_attention with the keys split across CTAs so a decode step fills the
+GPU, and the reference's prefill hand-off for q_len > 64 (:140-142). The split size is chosen
+per shape by the library's planner (bd3_decode_plan) instead of the fixed SPLIT_N; the
+constant is kept for callers that read it.
+"""
+
+import torch
+from torch import Tensor
+
+from bd3attn import ops
+from kernels.BlockSparseDecodeAttention import (  # noqa: F401
+    _cdt, _last_stride_1, block_sparse_decode_attention,
+)
+
+# keys per split of the reference (kernels/SplitKVDecodeAttention.py:13); informational here
+SPLIT_N = 256
+
+
+def split_kv_decode_attention(
+    q: Tensor,  # (batch, heads, q_len, head_dim): the last q_len positions
+    k: Tensor,  # (batch, heads, kv_len, head_dim)
+    v: Tensor,
+    block_size: int,
+) -> Tensor:
+    """Same result as block_sparse_decode_attention, with the keys split across CTAs."""
+    B, H, q_len, D = q.shape
+    if q_len > 64:
+        # prefill: many query tiles already fill the GPU
+        return block_sparse_decode_attention(q, k, v, block_size)
+    out_dtype = q.dtype
+    cdt = _cdt(q, k, v)
+    q, k, v = _last_stride_1(q.to(cdt)), _last_stride_1(k.to(cdt)), _last_stride_1(v.to(cdt))
+    if torch.compiler.is_compiling():
+        o = torch.ops.bd3.decode(q, k, v, int(block_size))
+    else:
+        o = ops.decode_raw(q, k, v, int(block_size))
+    return o if o.dtype == out_dtype else o.to(out_dtype)

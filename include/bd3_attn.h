@@ -1,0 +1,153 @@
+/* C ABI of the B200 BD3-LM attention library (libbd3attn.so).
+ *
+ * Plain pointers, sizes and strides; no framework types. Every entry point returns an int
+ * status (BD3_OK or one of the BD3_ERR_* codes) and leaves a message for bd3_last_error().
+ * Kernels are enqueued on `stream` (a cudaStream_t; NULL is the legacy default stream) and
+ * nothing synchronises: outputs are ready when the stream reaches that point.
+ *
+ * Tensors are 4-D (batch, heads, seq, head_dim) with head_dim contiguous. Each tensor
+ * argument is described by a pointer plus three element strides (batch, head, seq), passed
+ * in the `strides` array in argument order. Pointers and strides must be 16-byte aligned
+ * (the kernels read rows with TMA). head_dim must be 64.
+ *
+ * dtype codes: BD3_BF16, BD3_F16 (inputs); BD3_F32 is accepted as an output dtype of the
+ * decode entry points and of bd3_lse_merge.
+ */
+#ifndef BD3_ATTN_H_
+#define BD3_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BD3_API __attribute__((visibility("default")))
+#else
+#define BD3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  BD3_OK = 0,
+  BD3_ERR_INVALID = 1,     /* the reference would raise AssertionError on these arguments */
+  BD3_ERR_UNSUPPORTED = 2, /* valid for the reference, not supported here (e.g. head_dim) */
+  BD3_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed */
+  BD3_ERR_WORKSPACE = 4    /* workspace missing or smaller than the plan asks for */
+};
+enum { BD3_BF16 = 0, BD3_F16 = 1, BD3_F32 = 2 };
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+BD3_API int bd3_version(void);
+/* Message of the last failed call on this host thread ("" if none). */
+BD3_API const char* bd3_last_error(void);
+/* Sticky device-side status bits of the current device (1: a bounded wait inside a kernel
+ * ran out; 2: a kernel rejected its launch parameters). Synchronises the device. Clears the
+ * bits when `clear` is non-zero. Returns a negative value if the CUDA call itself failed. */
+BD3_API int bd3_device_status(int clear);
+
+/* ---------------------------------------------------------------------------------------
+ * Training attention forward under the BD3-LM block-diffusion mask.
+ * Replaces BlockSparseFlashAttention.forward (kernels/BlockSparseFlashAttention.py:466-506)
+ * and its kernel block_sparse_attention_fwd_kern (:76-172).
+ *   q, k, v, o: (B, H, 2n, 64); strides[12] = q, k, v, o (batch, head, seq) in elements.
+ *   lse:        (B, H, 2n) fp32, contiguous; per-row natural-log log-sum-exp (m + ln l).
+ * Requires n % 128 == 0 (the reference asserts n % BLOCK_M == 0 with BLOCK_M = 128).
+ */
+BD3_API int bd3_attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int64_t B,
+                 int64_t H, int64_t n, int64_t D, const int64_t* strides, int64_t block_size,
+                 int dtype, void* stream);
+
+/* Training attention backward: dQ, dK, dV from q, k, v, o, lse and dO.
+ * Replaces BlockSparseFlashAttention.backward (kernels/BlockSparseFlashAttention.py:509-562),
+ * i.e. the host Delta = rowsum(dO * O) (:525) and the kernels
+ * block_sparse_attention_bwd_dq_kern (:369-452) and block_sparse_attention_dk_dv_bwd_kern
+ * (:213-328). dK and dV are deterministic (one program owns each key tile, no atomics).
+ *   strides[24] = q, k, v, o, do, dq, dk, dv (batch, head, seq) in elements.
+ *   workspace: bd3_attn_bwd_workspace_size() bytes of device memory (Delta scratch).
+ * Requires n % 128 == 0 and n % block_size == 0 (the reference asserts both, :522, :548).
+ */
+BD3_API size_t bd3_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D);
+BD3_API int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                 const void* dout, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                 int64_t n, int64_t D, const int64_t* strides, int64_t block_size, int dtype,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Decode attention: the q_len queries attend kv_len keys under the block-causal rule
+ * (query row r sits at global position q_pos0 + r, key c at kv_pos0 + c; the row sees the key
+ * iff (q_pos0 + r) / bs >= (kv_pos0 + c) / bs). Pass q_pos0 = -1 for the reference's
+ * placement (the queries are the last q_len of the kv_len positions) and kv_pos0 = 0.
+ * Replaces split_kv_decode_attention (kernels/SplitKVDecodeAttention.py:130-171) and
+ * block_sparse_decode_attention (kernels/BlockSparseDecodeAttention.py:118-148):
+ * q_len <= 64 runs the split-KV kernel plus (when n_splits > 1) the LSE combine; longer
+ * query blocks (prefill) run the tcgen05 block-causal kernel and need n_splits == 1.
+ *   q: (B, H, q_len, 64); k, v: (B, H, kv_len, 64); o: (B, H, q_len, 64) in out_dtype.
+ *   strides[12] = q, k, v, o (batch, head, seq) in elements.
+ *   lse_out: optional (B*H, q_len) fp32 natural-log LSE of each row (NULL to skip).
+ * bd3_decode_plan() picks n_splits (pass the result back) and the workspace size.
+ */
+BD3_API int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t block_size,
+                    int64_t q_pos0, int64_t kv_pos0, int64_t* n_splits, size_t* workspace_bytes);
+BD3_API int bd3_decode_attn(const void* q, const void* k, const void* v, void* o, float* lse_out,
+                    int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t D,
+                    const int64_t* strides, int64_t block_size, int64_t q_pos0, int64_t kv_pos0,
+                    int64_t n_splits, int dtype, int out_dtype, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* Block-sparse decode over a per-(batch, head) list of live KV blocks of kv_block tokens
+ * (a multiple of 64). No counterpart kernel in the reference, whose oracle for it is
+ * model/modules.py:738 given the expanded (B, H, q_len, kv_len) mask; the block-causal rule
+ * above still applies inside the live blocks.
+ *   live_idx: (B*H, live_stride) int32 block indices, ascending; live_cnt: (B*H) int32.
+ *   q_len <= 64. bd3_decode_live_plan() gives n_splits and the workspace size.
+ */
+BD3_API int bd3_decode_live_plan(int64_t B, int64_t H, int64_t q_len, int64_t max_live,
+                         int64_t kv_block, int64_t* n_splits, size_t* workspace_bytes);
+BD3_API int bd3_decode_live_blocks(const void* q, const void* k, const void* v, void* o,
+                           float* lse_out, const int32_t* live_idx, const int32_t* live_cnt,
+                           int64_t live_stride, int64_t max_live, int64_t kv_block, int64_t B,
+                           int64_t H, int64_t q_len, int64_t kv_len, int64_t D,
+                           const int64_t* strides, int64_t block_size, int64_t n_splits,
+                           int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* LSE-weighted merge of G partial results over disjoint key sets (the math of
+ * split_kv_reduce_kern, kernels/SplitKVDecodeAttention.py:91-127; here also the merge of
+ * per-GPU partials after an all-gather for sequence-sharded decode).
+ *   parts: fp32, element (g, bh, r, d) at g*part_g + bh*part_bh + r*64 + d.
+ *   lses:  fp32, element (g, bh, r) at g*lse_g + bh*lse_bh + r.
+ *   o: (B, H, rows, 64) in out_dtype with o_strides[3]; lse_out optional (B*H, rows) fp32.
+ */
+BD3_API int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out, int64_t B,
+                  int64_t H, int64_t G, int64_t rows, int64_t D, int64_t part_g,
+                  int64_t part_bh, int64_t lse_g, int64_t lse_bh, const int64_t* o_strides,
+                  int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Per-kernel timing for benchmarks. While enabled, every launch is bracketed by a pair of
+ * CUDA events on its own stream (at most 8192 launches are kept). bd3_profile_collect()
+ * waits for them and writes, per kernel id (0 training forward, 1 prefill forward, 2 Delta,
+ * 3 dQ, 4 dK/dV, 5 decode, 6 decode combine), the summed milliseconds and launch counts to
+ * total_ms[7] and counts[7]; it returns 7 and forgets the recorded launches.
+ */
+BD3_API int bd3_profile_enable(int on);
+BD3_API int bd3_profile_collect(double* total_ms, int32_t* counts);
+
+/* ---------------------------------------------------------------------------------------
+ * Host-only introspection for tests (no GPU needed).
+ * bd3_debug_ranges: kind 0 forward/dQ key ranges, 1 dK/dV query ranges, 2 decode key ranges;
+ * writes (lo, hi, rule, shift) quadruples to out[16]; returns how many.
+ * bd3_debug_tiles: the library's tile sizes: out[0..5] = forward BM, BN; dK/dV BKV, BQ;
+ * decode BN; dQ BM.
+ */
+BD3_API int bd3_debug_ranges(int kind, int64_t start, int64_t tile_a, int64_t tile_b, int64_t n_or_qlen,
+                     int64_t kv_len, int64_t block_size, int32_t* out);
+BD3_API int bd3_debug_tiles(int32_t* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BD3_ATTN_H_ */

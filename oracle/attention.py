@@ -71,16 +71,17 @@ def live_block_mask(live: list[list[list[int]]], q_len: int, kv_len: int,
     return out
 
 
-def _as64(x) -> torch.Tensor:
+def _as64(x, dtype=torch.float64) -> torch.Tensor:
     if isinstance(x, np.ndarray):
         x = torch.from_numpy(x)
-    if x.requires_grad and x.dtype == torch.float64 and x.device.type == "cpu":
+    if x.requires_grad and x.dtype == dtype and x.device.type == "cpu":
         return x  # keep the autograd graph of attention_grads
-    return x.detach().to(device="cpu", dtype=torch.float64)
+    return x.detach().to(device="cpu", dtype=dtype)
 
 
-def attention(q, k, v, mask=None):
-    """(O, LSE) of softmax(q k^T / sqrt(d) masked) v in float64.
+def attention(q, k, v, mask=None, dtype=torch.float64, with_lse=True):
+    """(O, LSE) of softmax(q k^T / sqrt(d) masked) v, computed in ``dtype`` (float64 for the
+    parity checks; float32 is the reference's own CPU arithmetic, used for timing).
 
     O restates model/modules.py:738-771 (logits upcast before the product, masked scores
     set to -inf, a max-subtracted softmax, then P V). LSE is the per-row natural-log
@@ -89,29 +90,29 @@ def attention(q, k, v, mask=None):
 
     q: (..., Sq, D), k and v: (..., Sk, D); mask: bool broadcastable to (..., Sq, Sk).
     """
-    q, k, v = _as64(q), _as64(k), _as64(v)
+    q, k, v = _as64(q, dtype), _as64(k, dtype), _as64(v, dtype)
     scale = 1.0 / (q.shape[-1] ** 0.5)
     scores = torch.einsum("...qd,...kd->...qk", q, k) * scale
     if mask is not None:
         m = torch.as_tensor(np.asarray(mask)) if not torch.is_tensor(mask) else mask.cpu()
-        scores = torch.where(m, scores, torch.tensor(-torch.inf, dtype=torch.float64))
+        scores = torch.where(m, scores, torch.tensor(-torch.inf, dtype=dtype))
     z = scores - scores.amax(dim=-1, keepdim=True)
     e = torch.exp(z)
     p = e / e.sum(dim=-1, keepdim=True)
     out = torch.einsum("...qk,...kd->...qd", p, v)
-    lse = torch.logsumexp(scores, dim=-1)
+    lse = torch.logsumexp(scores, dim=-1) if with_lse else None
     return out, lse
 
 
-def attention_grads(q, k, v, do, mask=None):
+def attention_grads(q, k, v, do, mask=None, dtype=torch.float64):
     """(dQ, dK, dV) of attention(q, k, v, mask)[0] against the cotangent ``do``, by
     autograd through the float64 restatement (the oracle named for the training kernels'
     backward, kernels/BlockSparseFlashAttention.py:509-562)."""
-    q = _as64(q).requires_grad_(True)
-    k = _as64(k).requires_grad_(True)
-    v = _as64(v).requires_grad_(True)
-    out, _ = attention(q, k, v, mask)
-    dq, dk, dv = torch.autograd.grad(out, (q, k, v), _as64(do))
+    q = _as64(q, dtype).requires_grad_(True)
+    k = _as64(k, dtype).requires_grad_(True)
+    v = _as64(v, dtype).requires_grad_(True)
+    out, _ = attention(q, k, v, mask, dtype=dtype, with_lse=False)
+    dq, dk, dv = torch.autograd.grad(out, (q, k, v), _as64(do, dtype))
     return dq, dk, dv
 
 

@@ -1,0 +1,84 @@
+"""The C-ABI library loads, exports every symbol its header declares, and its tile-range
+code (the same __host__ __device__ functions the kernels run) equals the restatement of the
+reference formulas. No GPU needed: nothing here launches a kernel."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+from oracle import tile_ranges as tr
+
+HEADER = os.path.join(REPO, "include", "bd3_attn.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return re.findall(r"BD3_API\s+[\w\s\*]+?\b(bd3_\w+)\s*\(", text)
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    for must in ("bd3_attn_fwd", "bd3_attn_bwd", "bd3_decode_attn", "bd3_decode_live_blocks",
+                 "bd3_lse_merge", "bd3_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    from bd3attn._lib import LIB, SIGNATURES
+    for name in _declared():
+        assert hasattr(LIB, name), name
+        assert name in SIGNATURES, f"{name} has no ctypes signature"
+    assert LIB.bd3_version() >= 100
+
+
+def _lib_ranges(kind, start, a, b, nq, kv, bs):
+    from bd3attn._lib import LIB
+    out = (ctypes.c_int32 * 16)()
+    cnt = LIB.bd3_debug_ranges(kind, start, a, b, nq, kv, bs, out)
+    assert cnt > 0
+    return [tuple(out[4 * i:4 * i + 4]) for i in range(cnt)]
+
+
+def _tiles():
+    from bd3attn._lib import LIB
+    out = (ctypes.c_int32 * 8)()
+    LIB.bd3_debug_tiles(out)
+    return list(out[:6])
+
+
+@pytest.mark.parametrize("n,bs", [(128, 4), (128, 16), (1024, 16), (1024, 4), (512, 64),
+                                  (256, 256), (384, 128), (2048, 1024)])
+def test_fwd_and_dq_ranges_bit_exact(n, bs):
+    bm, bn, _, _, _, dq_bm = _tiles()
+    for q0 in range(0, 2 * n, bm):
+        assert _lib_ranges(0, q0, bm, bn, n, 0, bs) == tr.fwd_ranges(q0, bm, bn, n, bs)
+    for q0 in range(0, 2 * n, dq_bm):
+        assert _lib_ranges(0, q0, dq_bm, bn, n, 0, bs) == tr.dq_ranges(q0, dq_bm, bn, n, bs)
+
+
+@pytest.mark.parametrize("n,bs", [(128, 4), (128, 16), (1024, 16), (1024, 4), (512, 64),
+                                  (256, 256), (384, 128)])
+def test_dkdv_ranges_bit_exact(n, bs):
+    _, _, bkv, bq, _, _ = _tiles()
+    for k0 in range(0, 2 * n, bkv):
+        assert _lib_ranges(1, k0, bkv, bq, n, 0, bs) == tr.dkdv_ranges(k0, bkv, bq, n, bs)
+
+
+@pytest.mark.parametrize("q_len,kv_len,bs", [(3088, 3088, 16), (100, 1000, 64), (65, 65, 16),
+                                             (200, 4000, 16)])
+def test_prefill_ranges_bit_exact(q_len, kv_len, bs):
+    bm, bn = _tiles()[:2]
+    for q0 in range(0, q_len, bm):
+        assert _lib_ranges(2, q0, bm, bn, q_len, kv_len, bs) == \
+            tr.decode_ranges(q0, bm, bn, q_len, kv_len, bs)
+
+
+def test_library_tile_sizes_cover_masks():
+    """The tiling the kernels use is one the coverage tests in test_tile_ranges prove."""
+    bm, bn, bkv, bq, dec_bn, dq_bm = _tiles()
+    assert (bm, bn) in {(128, 64), (128, 128)}
+    assert (bkv, bq) in {(128, 32), (128, 64), (128, 128)}
+    assert dec_bn == 64 and dq_bm == 128

@@ -1,0 +1,150 @@
+"""Decode attention (split-KV, block-causal prefill, live blocks, LSE merge) on the GPU
+against the CPU oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import bf16_from_bits
+from gpu_util import LSE_TOL, O_TOL, assert_close, assert_device_ok, qkv
+
+pytestmark = pytest.mark.gpu
+
+SPLIT_CASES = [  # (B, H, q_len, kv_len, bs)
+    (1, 12, 16, 16, 16), (1, 12, 16, 1040, 16), (2, 3, 16, 4112, 16), (1, 2, 16, 300, 16),
+    (1, 2, 40, 200, 16), (1, 2, 64, 1000, 16), (2, 2, 7, 129, 4), (1, 1, 1, 1, 1),
+    (1, 2, 33, 64, 32), (3, 2, 16, 16400, 16),
+]
+
+
+@pytest.mark.parametrize("B,H,q_len,kv_len,bs", SPLIT_CASES)
+def test_split_kv_matches_oracle(B, H, q_len, kv_len, bs):
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    q, k, v = qkv(3, B, H, q_len, kv_len)
+    o = split_kv_decode_attention(q.cuda(), k.cuda(), v.cuda(), bs)
+    assert_device_ok()
+    ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, bs))
+    assert o.shape == q.shape and o.dtype == q.dtype
+    assert_close("O", o, ref, O_TOL)
+
+
+@pytest.mark.parametrize("n_splits", [1, 2, 3, 7, 17])
+def test_split_counts_and_lse(n_splits):
+    from bd3attn import ops
+    q, k, v = qkv(4, 2, 3, 16, 1040)
+    o, lse = ops.decode_raw(q.cuda(), k.cuda(), v.cuda(), 16, return_lse=True, n_splits=n_splits)
+    assert_device_ok()
+    ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(16, 1040, 16))
+    assert_close("O", o, ref, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+@pytest.mark.parametrize("B,H,q_len,kv_len,bs", [(1, 2, 65, 65, 16), (1, 2, 200, 1000, 16),
+                                                 (1, 3, 3088, 3088, 16), (2, 2, 300, 300, 64),
+                                                 (1, 1, 129, 4000, 16)])
+def test_prefill_matches_oracle(B, H, q_len, kv_len, bs):
+    from kernels.BlockSparseDecodeAttention import block_sparse_decode_attention
+    q, k, v = qkv(5, B, H, q_len, kv_len)
+    o = block_sparse_decode_attention(q.cuda(), k.cuda(), v.cuda(), bs)
+    assert_device_ok()
+    ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, bs))
+    assert_close("O", o, ref, O_TOL)
+
+
+def test_decode_against_reference_golden(golden):
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    tags = sorted({k.rsplit("_", 1)[0] for k in golden if k.startswith("decode_")})
+    for tag in tags:
+        bs = int(tag.split("_")[3][2:])
+        q, k, v = (bf16_from_bits(golden[f"{tag}_{x}"]) for x in ("q", "k", "v"))
+        o = split_kv_decode_attention(q.cuda(), k.cuda(), v.cuda(), bs)
+        assert_device_ok()
+        assert_close(tag, o, torch.from_numpy(golden[f"{tag}_o"]), O_TOL)
+
+
+def test_live_blocks_against_reference_golden(golden):
+    from kernels.BlockSparseDecodeAttention import block_sparse_live_decode_attention
+    q, k, v = (bf16_from_bits(golden[f"live_{x}"]) for x in ("q", "k", "v"))
+    live = torch.from_numpy(golden["live_blocks"]).int()
+    cnt = torch.full(live.shape[:2], live.shape[2], dtype=torch.int32)
+    o = block_sparse_live_decode_attention(q.cuda(), k.cuda(), v.cuda(), live.cuda(), cnt.cuda(),
+                                           64, 16)
+    assert_device_ok()
+    assert_close("O", o, torch.from_numpy(golden["live_o"]), O_TOL)
+
+
+@pytest.mark.parametrize("B,H,kv_len,n_blocks_live,kv_block", [(16, 12, 8192, 32, 64),
+                                                                (2, 3, 1000, 4, 128),
+                                                                (1, 2, 4096, 64, 64)])
+def test_live_blocks_matches_oracle(B, H, kv_len, n_blocks_live, kv_block):
+    from kernels.BlockSparseDecodeAttention import block_sparse_live_decode_attention
+    q_len, bs = 16, 16
+    q, k, v = qkv(6, B, H, q_len, kv_len)
+    rng = np.random.default_rng(0)
+    nb = -(-kv_len // kv_block)
+    live = np.zeros((B, H, n_blocks_live), dtype=np.int32)
+    cnt = np.zeros((B, H), dtype=np.int32)
+    for b in range(B):
+        for h in range(H):
+            c = int(rng.integers(1, n_blocks_live + 1))  # ragged counts per (b, h)
+            pick = rng.choice(nb - 1, size=c - 1, replace=False) if c > 1 else []
+            blocks = sorted(list(pick) + [nb - 1])  # the query block is always live
+            live[b, h, :c] = blocks
+            cnt[b, h] = c
+    o = block_sparse_live_decode_attention(q.cuda(), k.cuda(), v.cuda(),
+                                           torch.from_numpy(live).cuda(),
+                                           torch.from_numpy(cnt).cuda(), kv_block, bs)
+    assert_device_ok()
+    lists = [[live[b, h, :cnt[b, h]].tolist() for h in range(H)] for b in range(B)]
+    sub_b = min(B, 2)
+    mask = oracle.live_block_mask(lists[:sub_b], q_len, kv_len, kv_block, bs)
+    ref, _ = oracle.attention(q[:sub_b], k[:sub_b], v[:sub_b], mask)
+    assert_close("O", o[:sub_b], ref, O_TOL)
+
+
+def test_lse_merge_of_shards_equals_full():
+    """Sequence-sharded decode: per-shard partial (O fp32, LSE) then the merge kernel."""
+    from bd3attn import ops
+    B, H, q_len, kv_len, G, bs = 2, 3, 16, 4112, 4, 16
+    q, k, v = qkv(7, B, H, q_len, kv_len)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    edges = np.linspace(0, kv_len, G + 1).astype(int)
+    parts, lses = [], []
+    for g in range(G):
+        lo, hi = int(edges[g]), int(edges[g + 1])
+        o, l = ops.decode_raw(qd, kd[:, :, lo:hi], vd[:, :, lo:hi], bs, q_pos0=kv_len - q_len,
+                              kv_pos0=lo, out_dtype=torch.float32, return_lse=True)
+        parts.append(o)
+        lses.append(l)
+    o, lse = ops.lse_merge_raw(torch.stack(parts), torch.stack(lses), torch.bfloat16)
+    assert_device_ok()
+    ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, bs))
+    assert_close("O", o, ref, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+def test_fp32_output_and_inputs():
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    q, k, v = qkv(8, 1, 2, 16, 500, torch.float32)
+    o = split_kv_decode_attention(q.cuda(), k.cuda(), v.cuda(), 16)
+    assert_device_ok()
+    assert o.dtype == torch.float32
+    ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(16, 500, 16))
+    assert_close("O", o, ref, O_TOL)
+
+
+def test_non_contiguous_cache_views():
+    """k/v as views into a larger preallocated cache (length-sliced), q a strided view."""
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    q, k, v = qkv(9, 2, 3, 16, 2048)
+    kd = torch.zeros(2, 3, 4096, 64, dtype=torch.bfloat16, device="cuda")
+    vd = torch.zeros_like(kd)
+    kd[:, :, :2048] = k.cuda()
+    vd[:, :, :2048] = v.cuda()
+    qbig = torch.zeros(2, 16, 3, 64, dtype=torch.bfloat16, device="cuda")
+    qbig.copy_(q.cuda().transpose(1, 2))
+    o = split_kv_decode_attention(qbig.transpose(1, 2), kd[:, :, :2048], vd[:, :, :2048], 16)
+    assert_device_ok()
+    ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(16, 2048, 16))
+    assert_close("O", o, ref, O_TOL)

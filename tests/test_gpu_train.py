@@ -1,0 +1,121 @@
+"""Training attention (BD3-LM mask) forward and backward on the GPU against the CPU oracle."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import bf16_from_bits
+from gpu_util import GRAD_TOL, LSE_TOL, O_TOL, assert_close, assert_device_ok, qkv, randn
+
+pytestmark = pytest.mark.gpu
+
+CASES = [  # (B, H, n, block_size)
+    (1, 1, 128, 16), (1, 2, 128, 4), (2, 1, 256, 16), (1, 2, 256, 128), (1, 1, 512, 64),
+    (1, 1, 256, 256), (1, 2, 1024, 16), (1, 1, 1024, 4), (1, 1, 384, 32), (1, 1, 512, 1024 // 2),
+]
+
+
+def _run(B, H, n, bs, seed=0, dtype=torch.bfloat16):
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+    q, k, v = qkv(seed, B, H, 2 * n, 2 * n, dtype)
+    do = randn(torch.Generator().manual_seed(seed + 99), (B, H, 2 * n, 64), dtype)
+    qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = BlockSparseFlashAttention.apply(qd, kd, vd, bs)
+    dq, dk, dv = torch.autograd.grad(o, (qd, kd, vd), do.cuda())
+    assert_device_ok()
+    return (q, k, v, do), (o, dq, dk, dv)
+
+
+@pytest.mark.parametrize("B,H,n,bs", CASES)
+def test_forward_matches_oracle(B, H, n, bs):
+    from bd3attn import ops
+    q, k, v = qkv(1, B, H, 2 * n, 2 * n)
+    o, lse = ops.attn_fwd_raw(q.cuda(), k.cuda(), v.cuda(), bs)
+    assert_device_ok()
+    ref_o, ref_lse = oracle.attention(q, k, v, oracle.block_diff_mask(n, bs))
+    assert o.dtype == torch.bfloat16 and o.shape == q.shape
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+@pytest.mark.parametrize("B,H,n,bs", [c for c in CASES if c[2] <= 512] + [(1, 1, 1024, 16)])
+def test_backward_matches_oracle(B, H, n, bs):
+    (q, k, v, do), (o, dq, dk, dv) = _run(B, H, n, bs, seed=2)
+    mask = oracle.block_diff_mask(n, bs)
+    ref_o, _ = oracle.attention(q, k, v, mask)
+    rdq, rdk, rdv = oracle.attention_grads(q, k, v, do, mask)
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("dQ", dq, rdq, GRAD_TOL)
+    assert_close("dK", dk, rdk, GRAD_TOL)
+    assert_close("dV", dv, rdv, GRAD_TOL)
+
+
+def test_dkdv_deterministic():
+    _, (_, dq1, dk1, dv1) = _run(2, 2, 256, 16, seed=5)
+    _, (_, dq2, dk2, dv2) = _run(2, 2, 256, 16, seed=5)
+    assert torch.equal(dk1, dk2) and torch.equal(dv1, dv2) and torch.equal(dq1, dq2)
+
+
+@pytest.mark.parametrize("bs", [4, 16, 128])
+def test_against_reference_golden(golden, bs):
+    """Kernel vs the outputs the reference itself produced (fp32, on bf16-valued inputs)."""
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+    tag = f"train_n128_bs{bs}"
+    q, k, v, do = (bf16_from_bits(golden[f"{tag}_{x}"]) for x in ("q", "k", "v", "do"))
+    qd, kd, vd = (t.cuda().requires_grad_(True) for t in (q, k, v))
+    o = BlockSparseFlashAttention.apply(qd, kd, vd, bs)
+    dq, dk, dv = torch.autograd.grad(o, (qd, kd, vd), do.cuda())
+    assert_device_ok()
+    for name, got in (("o", o), ("dq", dq), ("dk", dk), ("dv", dv)):
+        assert_close(name, got, torch.from_numpy(golden[f"{tag}_{name}"]), O_TOL)
+
+
+def test_strided_inputs_like_the_model():
+    """q/k/v as views of a fused qkv projection: (B, S, 3*H*64) -> (B, H, S, 64) per tensor,
+    the layout model/modules.py:399-403 hands the attention (no copy is made)."""
+    from bd3attn import ops
+    B, H, n, bs = 2, 3, 256, 16
+    g = torch.Generator().manual_seed(4)
+    qkv_proj = randn(g, (B, 2 * n, 3 * H * 64))
+    t = qkv_proj.view(B, 2 * n, 3, H, 64).permute(2, 0, 3, 1, 4)
+    q, k, v = t[0], t[1], t[2]
+    dev = qkv_proj.cuda().view(B, 2 * n, 3, H, 64).permute(2, 0, 3, 1, 4)
+    o, lse = ops.attn_fwd_raw(dev[0], dev[1], dev[2], bs)
+    assert_device_ok()
+    ref_o, ref_lse = oracle.attention(q, k, v, oracle.block_diff_mask(n, bs))
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+def test_fp16_inputs():
+    from bd3attn import ops
+    q, k, v = qkv(8, 1, 2, 512, 512, torch.float16)
+    o, lse = ops.attn_fwd_raw(q.cuda(), k.cuda(), v.cuda(), 16)
+    assert_device_ok()
+    ref_o, ref_lse = oracle.attention(q, k, v, oracle.block_diff_mask(256, 16))
+    assert o.dtype == torch.float16
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+def test_fp32_inputs_config1_shape():
+    """BASELINE config 1 (B=2, H=12, n=1024, bs=16, fp32): computed in bf16 here."""
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+    q, k, v = qkv(9, 2, 12, 2048, 2048, torch.float32)
+    o = BlockSparseFlashAttention.apply(q.cuda(), k.cuda(), v.cuda(), 16)
+    assert_device_ok()
+    assert o.dtype == torch.float32
+    ref_o, _ = oracle.attention(q[:, :2], k[:, :2], v[:, :2], oracle.block_diff_mask(1024, 16))
+    assert_close("O", o[:, :2], ref_o, O_TOL)
+
+
+def test_reference_assertions():
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+    q = torch.zeros(1, 1, 200, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        BlockSparseFlashAttention.apply(q, q, q, 16)  # n = 100 is not a multiple of 128
+    q = torch.zeros(1, 1, 256, 64, device="cuda", dtype=torch.bfloat16)
+    k = torch.zeros(1, 1, 512, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(AssertionError):
+        BlockSparseFlashAttention.apply(q, k, k, 16)
