@@ -1,0 +1,90 @@
+"""Multi-GPU partitioning of the attention path (one process per GPU, torch.distributed).
+
+The reference is single-GPU; these are the two partitions the B200 build adds:
+
+* Batch x head sharding (training attention, decode, block-sparse decode, generation):
+  (batch, head) pairs are independent, so each rank takes a contiguous slice of them and
+  no collective touches the data path. ``bh_shard`` gives a rank's slice.
+
+* Sequence-sharded long-context decode: each rank holds a contiguous slice of the KV cache,
+  computes a partial attention (O in fp32, natural-log LSE) of the same query block over
+  its slice with the library's decode kernel, and one all-gather of the partials (NCCL over
+  NVLink on GPUs) feeds the LSE-weighted merge (bd3_lse_merge, the math of
+  kernels/SplitKVDecodeAttention.py:109-119). Peer memory is never read directly.
+
+``sharded_decode`` takes the local-partial and merge functions as arguments so the same
+partition logic runs on CPU ranks (gloo) in the tests with a checker in their place; on the
+GPU the defaults are the library's kernels and there is no fallback.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def bh_shard(B: int, H: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, stop) of the flattened (batch * head) index range owned by ``rank``; the
+    ranges tile [0, B*H) in rank order and differ in length by at most one."""
+    total = B * H
+    base, rem = divmod(total, world)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def seq_shard(kv_len: int, world: int, rank: int, align: int = 64) -> tuple[int, int]:
+    """[start, stop) of the KV positions held by ``rank``: contiguous slices in rank order,
+    boundaries on multiples of ``align`` (the decode kernel's key tile) except the end."""
+    tiles = -(-kv_len // align)
+    base, rem = divmod(tiles, world)
+    t0 = rank * base + min(rank, rem)
+    t1 = t0 + base + (1 if rank < rem else 0)
+    return min(t0 * align, kv_len), min(t1 * align, kv_len)
+
+
+def _gpu_partial(q, k, v, block_size, q_pos0, kv_pos0):
+    from bd3attn import ops
+    return ops.decode_raw(q, k, v, block_size, q_pos0=q_pos0, kv_pos0=kv_pos0,
+                          out_dtype=torch.float32, return_lse=True)
+
+
+def _gpu_merge(parts, lses, out_dtype):
+    from bd3attn import ops
+    return ops.lse_merge_raw(parts, lses, out_dtype)
+
+
+def sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
+                   block_size: int, kv_start: int, kv_len_total: int,
+                   group=None, out_dtype=None,
+                   partial_fn: Callable = _gpu_partial,
+                   merge_fn: Callable = _gpu_merge):
+    """Decode attention of ``q`` (B, H, q_len, 64) over a KV cache sharded by sequence.
+
+    k_local/v_local: (B, H, L_r, 64), this rank's keys at global positions
+    [kv_start, kv_start + L_r). The queries sit at the last q_len of kv_len_total positions
+    (the reference's placement). Returns (O (B, H, q_len, 64) in out_dtype, LSE), identical
+    on every rank. A rank whose slice no query can see contributes LSE = -inf.
+    """
+    world = dist.get_world_size(group)
+    B, H, q_len, D = q.shape
+    out_dtype = q.dtype if out_dtype is None else out_dtype
+    q_pos0 = kv_len_total - q_len
+    if k_local.shape[2] > 0:
+        o, lse = partial_fn(q, k_local, v_local, block_size, q_pos0, kv_start)
+        o = o.float()
+        lse = lse.float()
+    else:
+        o = torch.zeros(B, H, q_len, D, dtype=torch.float32, device=q.device)
+        lse = torch.full((B, H, q_len), float("-inf"), dtype=torch.float32, device=q.device)
+    # one all-gather of [O | LSE] per rank, packed so a single collective moves both
+    packed = torch.cat([o.reshape(B, H, q_len * D), lse.reshape(B, H, q_len)], dim=-1)
+    # ranks' blocks concatenated along dim 0 (the layout both NCCL and gloo produce)
+    gathered = torch.empty((world * B,) + tuple(packed.shape[1:]), dtype=packed.dtype,
+                           device=q.device)
+    dist.all_gather_into_tensor(gathered, packed.contiguous(), group=group)
+    gathered = gathered.view((world,) + tuple(packed.shape))
+    parts = gathered[..., : q_len * D].reshape(world, B, H, q_len, D)
+    lses = gathered[..., q_len * D:].reshape(world, B, H, q_len)
+    return merge_fn(parts.contiguous(), lses.contiguous(), out_dtype)

@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (ok) ok = mbar_wait(dq_done, 0);
+    ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
     if (ok) {
       tc_fence_after();
       uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
@@ -461,6 +462,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
     }
     if (ok && i > 0) ok = mbar_wait(mma_done, (i - 1) & 1);
+    ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
     if (ok) {
       tc_fence_after();
       const int key = k_start + row;  // accumulator lanes are keys

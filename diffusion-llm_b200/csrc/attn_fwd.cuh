@@ -280,8 +280,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     }
     // epilogue: wait for the last O += P V, normalise, store O and LSE
     if (ok && j > 0) ok = mbar_wait(o_done, (j - 1) & 1);
+    // every lane of the warp takes part in the TMEM loads (.sync.aligned); only the stores
+    // of rows past the end (a ragged last prefill tile) are skipped
+    ok = __all_sync(0xffffffffu, ok);
     const int rows_valid = (kMode == kTrain) ? 2 * p.n : p.q_len;
-    if (ok && qi < rows_valid) {
+    const bool store = qi < rows_valid;
+    if (ok) {
       tc_fence_after();
       const float inv_l = 1.f / l_run;
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
@@ -297,12 +301,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           packed[i] = pack2<kBF16>(__uint_as_float(r[2 * i]) * inv_l,
                                    __uint_as_float(r[2 * i + 1]) * inv_l);
         uint4* dst = reinterpret_cast<uint4*>(orow + c2 * 64);
+        if (store) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                              packed[4 * i + 3]);
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                                packed[4 * i + 3]);
+        }
       }
-      if (p.lse != nullptr)
+      if (store && p.lse != nullptr)
         p.lse[bb * p.lse_sb + hh * p.lse_sh + qi] = (m_use + __log2f(l_run)) * 0.69314718055994530942f;
     }
   }

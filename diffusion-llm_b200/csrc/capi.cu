@@ -158,7 +158,21 @@ int check_launch(const char* what) {
   return e == cudaSuccess ? BD3_OK : cuda_fail(e, what);
 }
 
+// Bind the current device's primary context to this host thread. A thread that has only
+// used another CUDA runtime (torch's autograd workers, for one) may have no current driver
+// context, and cuTensorMapEncodeTiled is a driver call.
+int ensure_context() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return BD3_OK;
+}
+
 int check_dims(int64_t B, int64_t H, int64_t D, int dtype) {
+  const int rc = ensure_context();
+  if (rc != BD3_OK) return rc;
   if (B < 1 || H < 1) return fail(BD3_ERR_INVALID, "batch and heads must be >= 1");
   if (D != 64) return fail(BD3_ERR_UNSUPPORTED, "head_dim must be 64 (got %lld)", (long long)D);
   if (dtype != BD3_BF16 && dtype != BD3_F16)
@@ -560,6 +574,7 @@ int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out
                   int64_t part_bh, int64_t lse_g, int64_t lse_bh, const int64_t* o_strides,
                   int out_dtype, void* stream) {
   if (B < 1 || H < 1 || G < 1 || rows < 1) return fail(BD3_ERR_INVALID, "merge sizes must be >= 1");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
   if (D != 64) return fail(BD3_ERR_UNSUPPORTED, "head_dim must be 64");
   if (out_dtype < BD3_BF16 || out_dtype > BD3_F32) return fail(BD3_ERR_INVALID, "bad out_dtype");
   if (reinterpret_cast<uintptr_t>(parts) % 16 || part_g % 4 || part_bh % 4)

@@ -28,7 +28,7 @@ enum : unsigned {
 };
 __device__ unsigned int g_bd3_status;
 
-constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s: far above any legitimate wait
+constexpr unsigned long long kWaitNs = 500000000ull;  // 0.5 s: far above any legitimate wait
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;

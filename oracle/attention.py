@@ -122,11 +122,15 @@ def lse_merge(o_parts, lse_parts):
     o_parts: (G, ..., Sq, D) outputs each normalised over its own keys; lse_parts:
     (G, ..., Sq) their log-sum-exps. Restates kernels/SplitKVDecodeAttention.py:109-119:
     weights exp(LSE_g - max_g LSE_g), normalised by their sum. Returns (O, LSE).
+    A partial that saw no key (LSE = -inf, O undefined) gets weight 0 and contributes
+    nothing, as a split of only masked keys does in the reference (its -1e6 masking leaves
+    such a split a finite LSE whose weight underflows to 0).
     """
     o = _as64(o_parts)
     lse = _as64(lse_parts)
     m = lse.amax(dim=0, keepdim=True)
     w = torch.exp(lse - m)
     den = w.sum(dim=0)
-    out = (w[..., None] * o).sum(dim=0) / den[..., None]
+    contrib = torch.where(w[..., None] > 0, w[..., None] * o, torch.zeros_like(o))
+    out = contrib.sum(dim=0) / den[..., None]
     return out, m[0] + torch.log(den)

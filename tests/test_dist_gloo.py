@@ -1,0 +1,94 @@
+"""Host-side logic of the multi-GPU partitions on world_size-2 gloo ranks (no GPU):
+the batch x head and sequence shard arithmetic, and the sequence-sharded decode's gather and
+merge, with the CPU oracle standing in for the device kernels."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from bd3attn.dist import bh_shard, seq_shard, sharded_decode
+
+
+@pytest.mark.parametrize("B,H,world", [(8, 12, 2), (8, 12, 8), (1, 12, 8), (3, 5, 4), (1, 1, 2)])
+def test_bh_shard_tiles_exactly(B, H, world):
+    seen = []
+    for r in range(world):
+        a, b = bh_shard(B, H, world, r)
+        seen.extend(range(a, b))
+    assert seen == list(range(B * H))
+
+
+@pytest.mark.parametrize("kv_len,world", [(65552, 8), (1000, 2), (64, 4), (130, 3)])
+def test_seq_shard_tiles_exactly(kv_len, world):
+    pos = []
+    for r in range(world):
+        a, b = seq_shard(kv_len, world, r)
+        assert a % 64 == 0
+        pos.extend(range(a, b))
+    assert pos == list(range(kv_len))
+
+
+def _oracle_partial(q, k, v, block_size, q_pos0, kv_pos0):
+    import oracle
+    q_len, kv_len = q.shape[2], k.shape[2]
+    qp = np.arange(q_pos0, q_pos0 + q_len)[:, None]
+    kp = np.arange(kv_pos0, kv_pos0 + kv_len)[None, :]
+    mask = (qp // block_size) >= (kp // block_size)
+    o, lse = oracle.attention(q, k, v, mask)
+    return o.float(), lse.float()
+
+
+def _oracle_merge(parts, lses, out_dtype):
+    import oracle
+    o, lse = oracle.lse_merge(parts, lses)
+    return o.to(out_dtype), lse.float()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(rank, world, port, kv_len, q_len, bs, result_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(2, 3, q_len, 64, generator=g)
+    k = torch.randn(2, 3, kv_len, 64, generator=g)
+    v = torch.randn(2, 3, kv_len, 64, generator=g)
+    a, b = seq_shard(kv_len, world, rank)
+    o, lse = sharded_decode(q, k[:, :, a:b], v[:, :, a:b], bs, a, kv_len,
+                            out_dtype=torch.float64, partial_fn=_oracle_partial,
+                            merge_fn=_oracle_merge)
+    if rank == 0:
+        torch.save((o, lse), result_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,kv_len,q_len,bs", [(2, 1040, 16, 16), (2, 300, 40, 16),
+                                                   (3, 130, 16, 16)])
+def test_sharded_decode_equals_full_attention(tmp_path, world, kv_len, q_len, bs):
+    import oracle
+    path = str(tmp_path / "out.pt")
+    mp.spawn(_worker, args=(world, _free_port(), kv_len, q_len, bs, path), nprocs=world,
+             join=True)
+    o, lse = torch.load(path)
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(2, 3, q_len, 64, generator=g)
+    k = torch.randn(2, 3, kv_len, 64, generator=g)
+    v = torch.randn(2, 3, kv_len, 64, generator=g)
+    ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, bs))
+    torch.testing.assert_close(o, ref, atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(lse.double(), ref_lse, atol=1e-5, rtol=1e-5)
