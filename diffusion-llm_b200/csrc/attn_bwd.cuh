@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       int vlo = -2147483647, vhi = 2147483647;
       if (rule != 0) train_row_interval(rule, shift, qi, p.n, p.bs, &vlo, &vhi);
       for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdDqBN, ++j) {
-        ok = mbar_wait(s_full, j & 1);
+        ok = mbar_wait_warp(s_full, j & 1);
         if (!ok) break;
         tc_fence_after();
         const int lo = vlo - s, hi = vhi - s;
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_arrive(ds_full);
       }
     }
-    if (ok) ok = mbar_wait(dq_done, 0);
+    if (ok) ok = mbar_wait_warp(dq_done, 0);
     ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
     if (ok) {
       tc_fence_after();
@@ -421,8 +421,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           lo -= k_start;
           hi -= k_start;
         }
-        ok = mbar_wait(s_full, i & 1);
-        if (ok && i > 0) ok = mbar_wait(mma_done, (i - 1) & 1);  // P/dS tiles are free
+        ok = mbar_wait_warp(s_full, i & 1);
+        if (ok && i > 0) ok = mbar_wait_warp(mma_done, (i - 1) & 1);  // P/dS tiles are free
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         mbar_arrive(p_full);
       }
     }
-    if (ok && i > 0) ok = mbar_wait(mma_done, (i - 1) & 1);
+    if (ok && i > 0) ok = mbar_wait_warp(mma_done, (i - 1) & 1);
     ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
     if (ok) {
       tc_fence_after();

@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
       for (int s = rg[ri].lo; s < rg[ri].hi; s += kFwdBN, ++j) {
         const int b = j & 1;
-        ok = mbar_wait(&s_full[b], (j >> 1) & 1);
+        ok = mbar_wait_warp(&s_full[b], (j >> 1) & 1);
         if (!ok) break;
         tc_fence_after();
         float x[128];
@@ -259,11 +259,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         l_run = l_run * alpha + sum;
         tmem_st_wait();
         if (j > 0) {
-          ok = mbar_wait(o_done, (j - 1) & 1);  // O += P_{j-1} V_{j-1} has landed
+          ok = mbar_wait_warp(o_done, (j - 1) & 1);  // O += P_{j-1} V_{j-1} has landed
           if (!ok) break;
           tc_fence_after();
         }
-        if (rescale) {
+        // the rescale's TMEM load/store is warp-collective: vote, and let the rows that do not
+        // need it multiply by alpha = 1
+        if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
           for (int c2 = 0; c2 < 2; ++c2) {
             uint32_t r[32];
@@ -279,7 +281,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       }
     }
     // epilogue: wait for the last O += P V, normalise, store O and LSE
-    if (ok && j > 0) ok = mbar_wait(o_done, (j - 1) & 1);
+    if (ok && j > 0) ok = mbar_wait_warp(o_done, (j - 1) & 1);
     // every lane of the warp takes part in the TMEM loads (.sync.aligned); only the stores
     // of rows past the end (a ragged last prefill tile) are skipped
     ok = __all_sync(0xffffffffu, ok);

@@ -90,6 +90,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+// Warp-uniform wait for warps that go on to issue warp-collective (.sync.aligned)
+// instructions: either every lane proceeds or none does, so a timeout cannot split a warp.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity));
+}
+
 // ---- TMA -----------------------------------------------------------------------------
 // 4-D tiled load of box {c0 (elements, innermost), c1, c2, c3} into shared memory,
 // completing on `bar` (transaction bytes). Never multicast.

@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(kDecThreads)
 
   // ---------------- consumers: warp w takes keys [16w, 16w+16) of every tile ----------------
   const int g = lane >> 2, tq = lane & 3;
-  bool ok = mbar_wait(q_full, 0);
+  bool ok = mbar_wait_warp(q_full, 0);
   uint32_t qa[kMB][4][4];  // A fragments: m-block, k-step (16 of D), regs
 #pragma unroll
   for (int mb = 0; mb < kMB; ++mb)
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kDecThreads)
     const int key = dec_tile_key<kLive>(p, bh, split, t, n_tiles);
     if (key < 0) break;
     const int st = t % kDecStages;
-    ok = mbar_wait(&full[st], (t / kDecStages) & 1);
+    ok = mbar_wait_warp(&full[st], (t / kDecStages) & 1);
     if (!ok) break;
     const uint32_t sk = sbase + DecSmem::kStage + st * 2 * kDecTile;
     const uint32_t sv = sk + kDecTile;

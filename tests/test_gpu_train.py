@@ -119,3 +119,45 @@ def test_reference_assertions():
     k = torch.zeros(1, 1, 512, 64, device="cuda", dtype=torch.bfloat16)
     with pytest.raises(AssertionError):
         BlockSparseFlashAttention.apply(q, k, k, 16)
+
+
+@pytest.mark.parametrize("bs", [4, 16])
+def test_forward_with_row_divergent_rescales(bs):
+    """Keys grow tile by tile, so the running maximum jumps by more than 2^8 for some rows of
+    a warp and not for others: the lazy-rescale path must stay warp-collective and exact."""
+    from bd3attn import ops
+    B, H, n = 1, 4, 1024
+    q, k, v = qkv(21, B, H, 2 * n, 2 * n)
+    ramp = torch.ones(2 * n)
+    ramp[n:] = torch.linspace(0.5, 3.0, n)       # clean keys: later blocks score higher
+    ramp[:n] = torch.linspace(0.5, 3.0, n)
+    k = (k.float() * ramp[None, None, :, None]).bfloat16()
+    o, lse = ops.attn_fwd_raw(q.cuda(), k.cuda(), v.cuda(), bs)
+    assert_device_ok()
+    ref_o, ref_lse = oracle.attention(q, k, v, oracle.block_diff_mask(n, bs))
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+@pytest.mark.parametrize("bs", [4, 16])
+def test_full_config2_size_runs_clean(bs):
+    """BASELINE config 2 at full size (B=8, H=12, n=1024): repeated fwd+bwd launches finish
+    with no bounded wait running out; two heads checked against the oracle."""
+    from bd3attn import ops
+    B, H, n = 8, 12, 1024
+    q, k, v = qkv(30 + bs, B, H, 2 * n, 2 * n)
+    do = randn(torch.Generator().manual_seed(31), (B, H, 2 * n, 64))
+    qd, kd, vd, dod = q.cuda(), k.cuda(), v.cuda(), do.cuda()
+    for _ in range(3):
+        o, lse = ops.attn_fwd_raw(qd, kd, vd, bs)
+        dq, dk, dv = ops.attn_bwd_raw(qd, kd, vd, o, lse, dod, bs)
+    assert_device_ok()
+    mask = oracle.block_diff_mask(n, bs)
+    sl = (slice(7, 8), slice(10, 12))
+    ref_o, ref_lse = oracle.attention(q[sl], k[sl], v[sl], mask)
+    assert_close("O", o[sl], ref_o, O_TOL)
+    assert_close("LSE", lse[sl], ref_lse, LSE_TOL)
+    rdq, rdk, rdv = oracle.attention_grads(q[sl], k[sl], v[sl], do[sl], mask)
+    assert_close("dQ", dq[sl], rdq, GRAD_TOL)
+    assert_close("dK", dk[sl], rdk, GRAD_TOL)
+    assert_close("dV", dv[sl], rdv, GRAD_TOL)
