@@ -23,7 +23,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -62,57 +61,66 @@ def load_peaks() -> dict:
 
 # ---------------------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    """SM clock and clock-event (throttle) reasons of one GPU, sampled through NVML every
+    2 ms by a background thread while the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
+    def __init__(self, device: int):
+        self.device = device
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
+        self.error = None
+
+    def _run(self):
+        import pynvml
+        while not self.stop.is_set():
+            try:
+                sm = pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((float(sm), int(rs)))
+            except Exception as e:  # keep the timed run going; report the error
+                self.error = repr(e)
+                return
+            time.sleep(0.002)
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._run, daemon=True)
+            self.thread.start()
+        except Exception as e:
+            self.error = repr(e)
+            self.thread = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        if getattr(self, "thread", None) is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower().startswith("active"):
+        import pynvml
+        reasons = set()
+        for _, rs in self.samples:
+            for name, const in self.REASONS:
+                if rs & getattr(pynvml, const, 0):
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
-        loaded = [s for s in sm if s >= 0.5 * max(sm)] or sm
-        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [s for s, _ in self.samples]
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(reasons), "samples": len(sm), "source": "nvml, 2 ms"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 # ---------------------------------------------------------------------------------------
@@ -164,13 +172,16 @@ def cpu_reference_step(n: int, bs: int, heads: int, gen_seed: int = 0) -> tuple[
     return dt, (f + b) * heads / H
 
 
-def cpu_baseline(reps: int = 3) -> dict:
+def cpu_baseline(budget_s: float = 10.0) -> dict:
+    """The reference's CPU path timed on this host's cores: repeated fwd+bwd of a B=1 slice
+    until about ``budget_s`` seconds of CPU work (at least 3 runs after a warm-up)."""
     torch.set_num_threads(os.cpu_count() or 1)
     cpu_reference_step(N_HALF, BS, H)  # warm-up
     times, flops = [], 0.0
-    for _ in range(reps):
+    while len(times) < 3 or sum(times) < budget_s:
         dt, flops = cpu_reference_step(N_HALF, BS, H)
         times.append(dt)
+    reps = len(times)
     med = statistics.median(times)
     return {"value": round(flops / med / 1e12, 6), "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port",
@@ -297,6 +308,13 @@ def run_ours(args) -> None:
     achieved = algo / (dom_ms * 1e-3) / 1e12
     launches = sum(c for _, c in prof.values())
 
+    if args.kernels_only:
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": UNIT,
+                              "kernels_ms_per_launch": {kk: round(t / c, 4)
+                                                        for kk, (t, c) in prof.items()}}))
+        return
+
     # bs = 4 (the other block size of config 2), same protocol, reported beside
     def step4():
         o, lse = ops.attn_fwd_raw(q, k, v, 4)
@@ -375,11 +393,40 @@ def main():
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
     ap.add_argument("--no-decode", action="store_true", help="skip the decode extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="time only the device steps (no bs=4 line, e2e, decode or CPU legs); "
+                         "the command the ncu captures run")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
+                         "the command the decode ncu captures run")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.decode_only:
+        run_decode_only(args)
     else:
         run_ours(args)
+
+
+def run_decode_only(args) -> None:
+    from bd3attn import ops
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    peaks = load_peaks()
+    g = torch.Generator().manual_seed(5)
+    b, kv = 8, 16384 + 16
+    q = torch.randn(b, H, 16, D, generator=g).bfloat16().to(dev)
+    k = torch.empty(b, H, kv, D, dtype=torch.bfloat16, device=dev).normal_()
+    v = torch.empty_like(k).normal_()
+    for _ in range(args.warmup):
+        ops.decode_raw(q, k, v, BS)
+    ms = time_steps(lambda: ops.decode_raw(q, k, v, BS), args.steps, l2)
+    by = b * H * (256 * kv + 4096)
+    t = statistics.median(ms)
+    print(json.dumps({"splitkv_b8_kv16k": {"us": round(t * 1e3, 2),
+                                           "GBps": round(by / t / 1e6, 1),
+                                           "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}}))
 
 
 if __name__ == "__main__":
