@@ -60,6 +60,16 @@ def load_peaks() -> dict:
 
 
 # ---------------------------------------------------------------------------------------
+def nvml_bus_id(device: int) -> str:
+    """NVML's "domain:bus:device.function" string of a CUDA device, from the integer PCI
+    fields torch reports (NVML would read a non-string argument as a char pointer)."""
+    p = torch.cuda.get_device_properties(device)
+    dom, bus, dev = p.pci_domain_id, p.pci_bus_id, p.pci_device_id
+    if not all(isinstance(x, int) for x in (dom, bus, dev)):
+        raise TypeError("PCI ids are not integers")
+    return f"{dom:08x}:{bus:02x}:{dev:02x}.0"
+
+
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons of one GPU, sampled through NVML every
     2 ms by a background thread while the timed region runs (read-only queries)."""
@@ -92,8 +102,7 @@ class ClockSampler:
         try:
             import pynvml
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(self.device).pci_bus_id
-            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(nvml_bus_id(self.device))
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
             self.stop = threading.Event()
             self.thread = threading.Thread(target=self._run, daemon=True)
