@@ -527,6 +527,75 @@ int bd3_decode_attn(const void* q, const void* k, const void* v, void* o, float*
                        out_dtype, workspace, workspace_bytes, st);
 }
 
+// ---------------------------------------------------------------------------------------
+// Decode without allocation.
+//
+// Some callers cannot call cudaMalloc: a serving engine that has reserved all of the
+// device's memory for its own allocator, or a decode loop that must not take the
+// synchronisation a cudaMalloc/cudaFree can imply. For them, bd3_decode_attn_noalloc runs the
+// same split-KV decode as bd3_decode_attn, but keeps its split partials in the fixed array
+// below instead of a caller-provided workspace. The caller still passes q, k, v and the
+// output buffers.
+//
+// The array is a file-scope __device__ variable: every GPU that loads this library holds its
+// kNoAllocScratchBytes until the process exits. In host code its name is only a host-side
+// stand-in, not a device address, so the device address is looked up with
+// cudaGetSymbolAddress on the first call on each device (with that device current) and kept.
+// That first call on a device therefore does a little set-up work; make it before any stream
+// capture. All calls share the one array and it keeps the last call's contents: nothing in it
+// needs to start at zero (every partial the combine step reads is written earlier in the same
+// call), but calls that overlap on the GPU (two streams, two host threads) race on it.
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(BD3_ERR_UNSUPPORTED, "device index %d too large", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return BD3_OK;
+}
+}  // namespace
+
+int bd3_decode_attn_noalloc(const void* q, const void* k, const void* v, void* o,
+                            float* lse_out, int64_t B, int64_t H, int64_t q_len,
+                            int64_t kv_len, int64_t D, const int64_t* strides,
+                            int64_t block_size, int64_t q_pos0, int64_t kv_pos0, int dtype,
+                            int out_dtype, void* stream) {
+  int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  if (q_len < 1 || q_len > 64)
+    return fail(BD3_ERR_UNSUPPORTED, "no-alloc decode handles 1 <= q_len <= 64 (got %lld)",
+                (long long)q_len);
+  int64_t n_splits = 1;
+  size_t need = 0;
+  if ((rc = bd3_decode_plan(B, H, q_len, kv_len, block_size, q_pos0, kv_pos0, &n_splits,
+                            &need)) != BD3_OK)
+    return rc;
+  if (need > kNoAllocScratchBytes)
+    return fail(BD3_ERR_UNSUPPORTED,
+                "no-alloc decode needs %zu bytes of scratch for %lld splits, more than its "
+                "fixed %zu bytes; use bd3_decode_attn with a workspace for this size",
+                need, (long long)n_splits, kNoAllocScratchBytes);
+  float* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch)) != BD3_OK) return rc;
+  return bd3_decode_attn(q, k, v, o, lse_out, B, H, q_len, kv_len, D, strides, block_size,
+                         q_pos0, kv_pos0, n_splits, dtype, out_dtype, scratch,
+                         kNoAllocScratchBytes, stream);
+}
+
 int bd3_decode_live_plan(int64_t B, int64_t H, int64_t q_len, int64_t max_live,
                          int64_t kv_block, int64_t* n_splits, size_t* workspace_bytes) {
   if (B < 1 || H < 1 || q_len < 1 || q_len > 64 || max_live < 1)

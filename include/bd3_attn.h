@@ -96,6 +96,21 @@ BD3_API int bd3_decode_attn(const void* q, const void* k, const void* v, void* o
                     int64_t n_splits, int dtype, int out_dtype, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Decode without allocation: the same result as bd3_decode_attn (split count from
+ * bd3_decode_plan) for callers that cannot call cudaMalloc, such as a serving engine whose
+ * allocator owns all device memory, or a decode loop that must not take the synchronisation
+ * an allocation can imply. No counterpart in the reference. The split partials live in a
+ * fixed 32 MiB array inside the library (held on every GPU that loads it until exit) instead
+ * of a workspace; sizes whose partials need more are rejected with BD3_ERR_UNSUPPORTED.
+ * The first call on a device looks the array's address up (set-up work; make it before any
+ * stream capture). Calls share the array, so calls that overlap on the GPU race.
+ * q_len <= 64; the other arguments are those of bd3_decode_attn. */
+BD3_API int bd3_decode_attn_noalloc(const void* q, const void* k, const void* v, void* o,
+                                    float* lse_out, int64_t B, int64_t H, int64_t q_len,
+                                    int64_t kv_len, int64_t D, const int64_t* strides,
+                                    int64_t block_size, int64_t q_pos0, int64_t kv_pos0,
+                                    int dtype, int out_dtype, void* stream);
+
 /* Block-sparse decode over a per-(batch, head) list of live KV blocks of kv_block tokens
  * (a multiple of 64). No counterpart kernel in the reference, whose oracle for it is
  * model/modules.py:738 given the expanded (B, H, q_len, kv_len) mask; the block-causal rule
