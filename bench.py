@@ -310,7 +310,8 @@ def run_ours(args) -> None:
     value = (fwd_f + bwd_f) * args.steps * world / (total_ms * 1e-3) / 1e12
 
     # roofline of the dominant kernel: algorithmic FLOPs per launch / its mean duration
-    per_launch_mm = {"attn_fwd": 2, "bwd_dq": 3, "bwd_dkdv": 4}  # nnz-restricted matmuls
+    # nnz-restricted matmuls per launch: forward QK^T, PV; fused backward S, dP, dV, dK, dQ
+    per_launch_mm = {"attn_fwd": 2, "bwd_fused": 5}
     dom = max((kname for kname in prof if kname in per_launch_mm), key=lambda kk: prof[kk][0])
     dom_ms = prof[dom][0] / prof[dom][1]
     algo = per_launch_mm[dom] * 2.0 * D * nnz(N_HALF, BS) * B * H

@@ -211,8 +211,8 @@ def _(q, k, v, block_size):
 
 
 # ---------------------------------------------------------------------------------------
-PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_delta", "bwd_dq", "bwd_dkdv", "decode",
-                   "decode_combine")
+PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_prep", "bwd_dq_convert", "bwd_fused",
+                   "decode", "decode_combine")
 
 
 def profile_enable(on: bool = True) -> None:

@@ -1,22 +1,32 @@
 // Block-sparse attention backward on tcgen05 tensor cores (sm_100a).
 //
-// Replaces BlockSparseFlashAttention.backward (kernels/BlockSparseFlashAttention.py:509-562):
-//   bwd_delta_kernel   Delta = rowsum(dO * O) in fp32 (the host op at :525)
-//   bwd_dq_kernel      dQ = scale * sum_j dS_j K_j over the forward's key ranges
-//                      (block_sparse_attention_bwd_dq_kern, :369-452)
-//   bwd_dkdv_kernel    dV = sum_i P_i^T dO_i, dK = scale * sum_i dS_i^T Q_i over the query
-//                      ranges of one key tile (block_sparse_attention_dk_dv_bwd_kern, :213-328);
-//                      one CTA owns each key tile, so dK and dV are deterministic.
-// with P = exp(scale * Q K^T - LSE) masked to 0 and dS = P * (dO V^T - Delta).
+// Replaces BlockSparseFlashAttention.backward (kernels/BlockSparseFlashAttention.py:509-562),
+// i.e. the host Delta = rowsum(dO * O) (:525) and the kernels block_sparse_attention_bwd_dq_kern
+// (:369-452) and block_sparse_attention_dk_dv_bwd_kern (:213-328), with three launches:
 //
-// Both tile kernels compute S = Q K^T and dP = dO V^T with the query rows on the TMEM lanes
-// (M = 128 queries, N = 128 keys), so every softmax thread owns one query row and keeps that
-// row's LSE and Delta in registers.
-//   dQ kernel:   dS is written back into the S columns of TMEM as packed 16-bit pairs and
-//                consumed by a TS-form MMA: dQ[q, :] += dS[q, keys] K[keys, :].
-//   dK/dV kernel: P and dS are written to shared memory as [query][key] 128-byte-swizzled
-//                tiles; the same bytes are the MN-major A operand of dV += P^T dO and
-//                dK += dS^T Q (M = 128 keys, N = 64, K = 128 queries).
+//   bwd_prep_kernel     Delta = rowsum(dO * O) and LSE * log2(e) per query row (fp32), and
+//                       zeroes the fp32 dQ accumulator.
+//   bwd_fused_kernel    one CTA per (batch*head, 128-key tile), stepping over the query ranges
+//                       that see the tile (the reference's dK/dV ranges, :274-325):
+//                         S^T  = K Q_i^T,  dP^T = V dO_i^T          (SS MMAs, keys on TMEM lanes)
+//                         P^T  = exp2(S^T * scale*log2e - L2[q]) masked to 0,
+//                         dS^T = P^T * (dP^T - Delta[q])            (element-wise, thread = key)
+//                         dV  += P^T dO_i,  dK += dS^T Q_i          (TS MMAs: P^T, dS^T in TMEM)
+//                         dQ_i = dS_i K                              (SS MMA from a smem dS tile)
+//                       dV and dK accumulate in TMEM and are written once, so they are
+//                       deterministic; each dQ_i is added to the fp32 accumulator by a reducer
+//                       warpgroup with vector reductions (red.global.add.v4.f32).
+//   bwd_dq_convert_kernel  dQ = scale * accumulator, in the input dtype.
+//
+// Roles in the fused kernel (320 threads):
+//   warps 0-3  element-wise: thread t owns key row t of the tile (TMEM lane t)
+//   warps 4-7  dQ reducer: thread t owns query row t of dQ_i (TMEM lane t)
+//   warp 8     TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
+//   warp 9     TMEM owner and UMMA issuer
+// TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ_i [384,448);
+// P^T (packed 16-bit) overwrites S^T [0,64) and dS^T overwrites dP^T [128,192).
+// dS for the dQ MMA lives in shared memory as [query half][key row][64 queries] with the
+// 128-byte swizzle, which is the MN-major A operand (M = queries, K = keys).
 #pragma once
 
 #include "attn_fwd.cuh"
@@ -25,31 +35,47 @@
 
 namespace bd3 {
 
-constexpr int kBwdBKV = 128;   // dK/dV: keys per CTA
-constexpr int kBwdBQ = 128;    // dK/dV: queries per step
-constexpr int kBwdDqBM = 128;  // dQ: queries per CTA
-constexpr int kBwdDqBN = 128;  // dQ: keys per step
+constexpr int kBwdBKV = 128;  // keys per CTA
+constexpr int kBwdBQ = 128;   // queries per step
 constexpr int kBwdStages = 2;
-constexpr int kBwdThreads = 192;
+constexpr int kBwdThreads = 320;
 
 struct BwdParams {
   const void* o;
   const void* dout;
-  const float* lse;      // (B, H, 2n)
-  float* delta;          // (B, H, 2n), written by bwd_delta_kernel
+  const float* lse;      // (B, H, 2n), natural log
+  float* delta;          // (B, H, 2n), written by bwd_prep_kernel
+  float* lse2;           // (B, H, 2n), LSE * log2(e), written by bwd_prep_kernel
+  float* dq_acc;         // (B, H, 2n, 64) fp32, zeroed by bwd_prep_kernel
   void* dq;
   void* dk;
   void* dv;
   long long o_sb, o_sh, o_ss, do_sb, do_sh, do_ss;
   long long dq_sb, dq_sh, dq_ss, dk_sb, dk_sh, dk_ss, dv_sb, dv_sh, dv_ss;
   int H, n, bs;
-  int num_tiles;         // query tiles (dQ) or key tiles (dK/dV) per (batch, head)
+  int num_tiles;         // key tiles per (batch, head)
   float scale, scale_log2;
 };
 
-// Delta[bh, r] = sum_d dO[r, d] * O[r, d]; 8 threads per row, 16 bytes each.
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Delta, LSE*log2(e) and the dQ accumulator's zeroing; 8 threads per query row.
 template <bool kBF16>
-__global__ void __launch_bounds__(256) bwd_delta_kernel(const BwdParams p, int rows_total) {
+__global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdParams p, int rows_total) {
   const int gid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gid >> 3, part = gid & 7;
   float acc = 0.f;
@@ -68,11 +94,35 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const BwdParams p, int r
       acc = fmaf(x.x, y.x, acc);
       acc = fmaf(x.y, y.y, acc);
     }
+    float4* z = reinterpret_cast<float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
+    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-  if (row < rows_total && part == 0) p.delta[row] = acc;
+  if (row < rows_total && part == 0) {
+    p.delta[row] = acc;
+    p.lse2[row] = p.lse[row] * 1.4426950408889634f;
+  }
+}
+
+// dQ = scale * accumulator in the output dtype; 8 threads per query row.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const BwdParams p, int rows_total) {
+  const int gid = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = gid >> 3, part = gid & 7;
+  if (row >= rows_total) return;
+  const int S = 2 * p.n;
+  const int bh = row / S, r = row % S;
+  const int bb = bh / p.H, hh = bh % p.H;
+  const float4* src = reinterpret_cast<const float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
+  const float4 x = src[0], y = src[1];
+  const float s = p.scale;
+  *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.dq) + bb * p.dq_sb + hh * p.dq_sh +
+                            r * p.dq_ss + part * 8) =
+      make_uint4(pack2<kBF16>(x.x * s, x.y * s), pack2<kBF16>(x.z * s, x.w * s),
+                 pack2<kBF16>(y.x * s, y.y * s), pack2<kBF16>(y.z * s, y.w * s));
 }
 
 // Store 64 fp32 accumulator columns of one row (read from TMEM) as 16-bit values * mul.
@@ -93,226 +143,53 @@ __device__ __forceinline__ void store_row64(uint32_t taddr, void* dst, float mul
   }
 }
 
-// ---------------------------------------------------------------------------------------
-// dQ: one CTA per (batch*head, 128-query tile), stepping over the forward's key ranges.
-struct DqSmem {
-  static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kDO = kQ + kTile16;
-  static constexpr uint32_t kK = kDO + kTile16;
-  static constexpr uint32_t kV = kK + kBwdStages * kTile16;
-  static constexpr uint32_t kBar = kV + kBwdStages * kTile16;
-  // qo_full, kv_full[S], kv_empty[S], s_full, ds_full, dq_done
-  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 3;
-  static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
-  static constexpr uint32_t kAlloc = kTmemSlot + 16 + 1024;
-};
-
-template <bool kBF16>
-__global__ void __launch_bounds__(kBwdThreads, 1)
-    bwd_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                  const BwdParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DqSmem::kBar);
-  uint64_t* qo_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = bars + 1 + kBwdStages;
-  uint64_t* s_full = bars + 1 + 2 * kBwdStages;
-  uint64_t* ds_full = s_full + 1;
-  uint64_t* dq_done = s_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + DqSmem::kTmemSlot);
-
-  const int warp = static_cast<int>(warp_id());
-  const int BH = gridDim.x / p.num_tiles;
-  const int bh = blockIdx.x % BH;
-  const int q_tile = fwd_tile_order(blockIdx.x / BH, p.num_tiles, kTrain);
-  const int q_start = q_tile * kBwdDqBM;
-  const int bb = bh / p.H, hh = bh % p.H;
-  Range rg[3];
-  const int nr = fwd_ranges(q_start, kBwdDqBM, kBwdDqBN, p.n, p.bs, rg);
-
-  if (threadIdx.x == 0) {
-    mbar_init(qo_full, 1);
-    for (int s = 0; s < kBwdStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    mbar_init(s_full, 1);
-    mbar_init(ds_full, 128);
-    mbar_init(dq_done, 1);
-    fence_mbar_init();
-  }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 4) {
-    if (elect_one()) {
-      bool ok = true;
-      mbar_expect_tx(qo_full, 2 * kTile16);
-      tma_load_4d(&tm_q, qo_full, smem + DqSmem::kQ, 0, q_start, hh, bb);
-      tma_load_4d(&tm_do, qo_full, smem + DqSmem::kDO, 0, q_start, hh, bb);
-      int j = 0;
-      for (int ri = 0; ri < nr && ok; ++ri)
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdDqBN, ++j) {
-          const int st = j % kBwdStages;
-          if (j >= kBwdStages) ok = mbar_wait(&kv_empty[st], ((j / kBwdStages) - 1) & 1);
-          if (!ok) break;
-          mbar_expect_tx(&kv_full[st], 2 * kTile16);
-          tma_load_4d(&tm_k, &kv_full[st], smem + DqSmem::kK + st * kTile16, 0, s, hh, bb);
-          tma_load_4d(&tm_v, &kv_full[st], smem + DqSmem::kV + st * kTile16, 0, s, hh, bb);
-        }
-    }
-    __syncwarp();
-  } else if (warp == 5) {
-    if (elect_one()) {
-      constexpr uint32_t idesc_s = idesc_f16(128, 128, false, false, kBF16);
-      constexpr uint32_t idesc_dq = idesc_f16(128, 64, false, true, kBF16);
-      const uint32_t sbase = smem_u32(smem);
-      const uint64_t qdesc = sw128_desc(sbase + DqSmem::kQ, 16, 1024);
-      const uint64_t dodesc = sw128_desc(sbase + DqSmem::kDO, 16, 1024);
-      bool ok = mbar_wait(qo_full, 0);
-      int j = 0;
-      for (int ri = 0; ri < nr && ok; ++ri)
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdDqBN, ++j) {
-          const int st = j % kBwdStages;
-          ok = mbar_wait(&kv_full[st], (j / kBwdStages) & 1);
-          if (!ok) break;
-          tc_fence_after();
-          const uint64_t kdesc = sw128_desc(sbase + DqSmem::kK + st * kTile16, 16, 1024);
-          const uint64_t vdesc = sw128_desc(sbase + DqSmem::kV + st * kTile16, 16, 1024);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem, qdesc + kk * 2, kdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + 128, dodesc + kk * 2, vdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
-          umma_commit(s_full);
-          ok = mbar_wait(ds_full, j & 1);
-          if (!ok) break;
-          tc_fence_after();
-          const uint64_t kmn = sw128_desc(sbase + DqSmem::kK + st * kTile16, kTile16, 1024);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_ts(tmem + 256, tmem + kk * 8, kmn + ((kk * 2048) >> 4), idesc_dq,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&kv_empty[st]);
-        }
-      umma_commit(dq_done);
-    }
-    __syncwarp();
-  } else {
-    const int row = threadIdx.x;
-    const int qi = q_start + row;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const long long lrow = static_cast<long long>(bh) * 2 * p.n + qi;
-    const float L2 = p.lse[lrow] * 1.4426950408889634f;
-    const float Dl = p.delta[lrow];
-    bool ok = true;
-    int j = 0;
-    for (int ri = 0; ri < nr && ok; ++ri) {
-      const int rule = rg[ri].rule, shift = rg[ri].shift;
-      int vlo = -2147483647, vhi = 2147483647;
-      if (rule != 0) train_row_interval(rule, shift, qi, p.n, p.bs, &vlo, &vhi);
-      for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdDqBN, ++j) {
-        ok = mbar_wait_warp(s_full, j & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const int lo = vlo - s, hi = vhi - s;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + c * 32, sr);
-          tmem_ld32(tmem + lane_base + 128 + c * 32, dr);
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float ds2[2];
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int col = c * 32 + 2 * i + h;
-              float pv = ex2(fmaf(__uint_as_float(sr[2 * i + h]), p.scale_log2, -L2));
-              if (rule != 0 && (col < lo || col >= hi)) pv = 0.f;
-              ds2[h] = pv * (__uint_as_float(dr[2 * i + h]) - Dl);
-            }
-            pk[i] = pack2<kBF16>(ds2[0], ds2[1]);
-          }
-          tmem_st16(tmem + lane_base + c * 16, pk);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(ds_full);
-      }
-    }
-    if (ok) ok = mbar_wait_warp(dq_done, 0);
-    ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
-    if (ok) {
-      tc_fence_after();
-      uint8_t* dst = reinterpret_cast<uint8_t*>(p.dq) +
-                     2 * (bb * p.dq_sb + hh * p.dq_sh + static_cast<long long>(qi) * p.dq_ss);
-      store_row64<kBF16>(tmem + lane_base + 256, dst, p.scale);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 5) {
-    tc_fence_after();
-    tmem_dealloc(tmem, 512);
-  }
-}
-
-// ---------------------------------------------------------------------------------------
-// dK/dV: one CTA per (batch*head, 128-key tile), stepping over the query ranges that see it.
-struct DkdvSmem {
+struct BwdSmem {
   static constexpr uint32_t kK = 0;
   static constexpr uint32_t kV = kK + kTile16;
-  static constexpr uint32_t kQ = kV + kTile16;
-  static constexpr uint32_t kDO = kQ + kBwdStages * kTile16;
-  static constexpr uint32_t kP = kDO + kBwdStages * kTile16;   // [2 key halves][128 q][128 B]
-  static constexpr uint32_t kDS = kP + 2 * kTile16;
-  static constexpr uint32_t kBar = kDS + 2 * kTile16;
-  // kv_full, qd_full[S], qd_empty[S], s_full, p_full, mma_done
-  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 3;
+  static constexpr uint32_t kQ = kV + kTile16;                  // [stage]
+  static constexpr uint32_t kDO = kQ + kBwdStages * kTile16;    // [stage]
+  static constexpr uint32_t kDS = kDO + kBwdStages * kTile16;   // [query half][128 keys][128 B]
+  static constexpr uint32_t kVec = kDS + 2 * kTile16;           // [stage][L2 128 | Delta 128]
+  static constexpr uint32_t kBar = kVec + kBwdStages * 1024;
+  // kv_full, qd_full[S], qd_empty[S], s_full, p_full, dq_full, dq_empty, acc_done
+  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 5;
   static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
   static constexpr uint32_t kAlloc = kTmemSlot + 16 + 1024;
 };
 
 // Key tile processed by linear CTA index t: the clean key tiles near the start of the clean
-// copy are seen by the most query tiles, so they go first.
-__device__ __forceinline__ int dkdv_tile_order(int t, int num_tiles) {
+// copy are seen by the most query tiles, so they go first; noisy tiles (one step) last.
+__device__ __forceinline__ int bwd_tile_order(int t, int num_tiles) {
   const int half = num_tiles / 2;
-  if (t < half) return half + t;  // clean tiles, heaviest (lowest index) first
-  return t - half;                // noisy tiles: one query tile each
+  if (t < half) return half + t;
+  return t - half;
 }
 
 template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
-    bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const BwdParams p) {
+    bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                     const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DkdvSmem::kBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BwdSmem::kBar);
   uint64_t* kv_full = bars;
   uint64_t* qd_full = bars + 1;
   uint64_t* qd_empty = bars + 1 + kBwdStages;
   uint64_t* s_full = bars + 1 + 2 * kBwdStages;
   uint64_t* p_full = s_full + 1;
-  uint64_t* mma_done = s_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + DkdvSmem::kTmemSlot);
+  uint64_t* dq_full = s_full + 2;
+  uint64_t* dq_empty = s_full + 3;
+  uint64_t* acc_done = s_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BwdSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
   const int BH = gridDim.x / p.num_tiles;
   const int bh = blockIdx.x % BH;
-  const int k_tile = dkdv_tile_order(blockIdx.x / BH, p.num_tiles);
+  const int k_tile = bwd_tile_order(blockIdx.x / BH, p.num_tiles);
   const int k_start = k_tile * kBwdBKV;
   const int bb = bh / p.H, hh = bh % p.H;
+  const long long row0 = static_cast<long long>(bh) * 2 * p.n;  // first row of this (b, h)
   Range rg[4];
   const int nr = dkdv_ranges(k_start, kBwdBKV, kBwdBQ, p.n, p.bs, rg);
 
@@ -324,10 +201,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
     mbar_init(s_full, 1);
     mbar_init(p_full, 128);
-    mbar_init(mma_done, 1);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 128);
+    mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -335,35 +214,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S [0,128), dP [128,256), dV [256,320), dK [320,384)
+  constexpr uint32_t tS = 0, tDP = 128, tDV = 256, tDK = 320, tDQ = 384;
 
-  if (warp == 4) {
+  if (warp == 8) {
+    // ---------------- TMA producer ----------------
     if (elect_one()) {
       bool ok = true;
       mbar_expect_tx(kv_full, 2 * kTile16);
-      tma_load_4d(&tm_k, kv_full, smem + DkdvSmem::kK, 0, k_start, hh, bb);
-      tma_load_4d(&tm_v, kv_full, smem + DkdvSmem::kV, 0, k_start, hh, bb);
+      tma_load_4d(&tm_k, kv_full, smem + BwdSmem::kK, 0, k_start, hh, bb);
+      tma_load_4d(&tm_v, kv_full, smem + BwdSmem::kV, 0, k_start, hh, bb);
       int i = 0;
       for (int ri = 0; ri < nr && ok; ++ri)
         for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdBQ, ++i) {
           const int st = i % kBwdStages;
           if (i >= kBwdStages) ok = mbar_wait(&qd_empty[st], ((i / kBwdStages) - 1) & 1);
           if (!ok) break;
-          mbar_expect_tx(&qd_full[st], 2 * kTile16);
-          tma_load_4d(&tm_q, &qd_full[st], smem + DkdvSmem::kQ + st * kTile16, 0, s, hh, bb);
-          tma_load_4d(&tm_do, &qd_full[st], smem + DkdvSmem::kDO + st * kTile16, 0, s, hh, bb);
+          mbar_expect_tx(&qd_full[st], 2 * kTile16 + 1024);
+          tma_load_4d(&tm_q, &qd_full[st], smem + BwdSmem::kQ + st * kTile16, 0, s, hh, bb);
+          tma_load_4d(&tm_do, &qd_full[st], smem + BwdSmem::kDO + st * kTile16, 0, s, hh, bb);
+          uint8_t* vec = smem + BwdSmem::kVec + st * 1024;
+          bulk_load(vec, p.lse2 + row0 + s, 512, &qd_full[st]);
+          bulk_load(vec + 512, p.delta + row0 + s, 512, &qd_full[st]);
         }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
+    // ---------------- UMMA issuer ----------------
     if (elect_one()) {
       constexpr uint32_t idesc_s = idesc_f16(128, 128, false, false, kBF16);
-      constexpr uint32_t idesc_acc = idesc_f16(128, 64, true, true, kBF16);
+      constexpr uint32_t idesc_ts = idesc_f16(128, 64, false, true, kBF16);
+      constexpr uint32_t idesc_dq = idesc_f16(128, 64, true, true, kBF16);
       const uint32_t sbase = smem_u32(smem);
-      const uint64_t kdesc = sw128_desc(sbase + DkdvSmem::kK, 16, 1024);
-      const uint64_t vdesc = sw128_desc(sbase + DkdvSmem::kV, 16, 1024);
-      const uint64_t pdesc = sw128_desc(sbase + DkdvSmem::kP, kTile16, 1024);
-      const uint64_t dsdesc = sw128_desc(sbase + DkdvSmem::kDS, kTile16, 1024);
+      const uint64_t kdesc = sw128_desc(sbase + BwdSmem::kK, 16, 1024);
+      const uint64_t vdesc = sw128_desc(sbase + BwdSmem::kV, 16, 1024);
+      const uint64_t kmn = sw128_desc(sbase + BwdSmem::kK, kTile16, 1024);
+      const uint64_t dsdesc = sw128_desc(sbase + BwdSmem::kDS, kTile16, 1024);
       bool ok = mbar_wait(kv_full, 0);
       int i = 0;
       for (int ri = 0; ri < nr && ok; ++ri)
@@ -372,16 +257,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = mbar_wait(&qd_full[st], (i / kBwdStages) & 1);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t qa = sbase + DkdvSmem::kQ + st * kTile16;
-          const uint32_t da = sbase + DkdvSmem::kDO + st * kTile16;
+          const uint32_t qa = sbase + BwdSmem::kQ + st * kTile16;
+          const uint32_t da = sbase + BwdSmem::kDO + st * kTile16;
           const uint64_t qdesc = sw128_desc(qa, 16, 1024);
           const uint64_t dodesc = sw128_desc(da, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem, qdesc + kk * 2, kdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+            umma_ss(tmem + tS, kdesc + kk * 2, qdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + 128, dodesc + kk * 2, vdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+            umma_ss(tmem + tDP, vdesc + kk * 2, dodesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
           umma_commit(s_full);
           ok = mbar_wait(p_full, i & 1);
           if (!ok) break;
@@ -390,89 +275,126 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint64_t qmn = sw128_desc(qa, kTile16, 1024);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_ss(tmem + 256, pdesc + ((kk * 2048) >> 4), domn + ((kk * 2048) >> 4), idesc_acc,
+            umma_ts(tmem + tDV, tmem + tS + kk * 8, domn + ((kk * 2048) >> 4), idesc_ts,
                     (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            umma_ss(tmem + 320, dsdesc + ((kk * 2048) >> 4), qmn + ((kk * 2048) >> 4), idesc_acc,
+            umma_ts(tmem + tDK, tmem + tDP + kk * 8, qmn + ((kk * 2048) >> 4), idesc_ts,
                     (i > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(mma_done);
           umma_commit(&qd_empty[st]);
+          if (i > 0) {
+            ok = mbar_wait(dq_empty, (i - 1) & 1);  // the reducer has read dQ_{i-1}
+            if (!ok) break;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_ss(tmem + tDQ, dsdesc + ((kk * 2048) >> 4), kmn + ((kk * 2048) >> 4), idesc_dq,
+                    kk > 0 ? 1u : 0u);
+          umma_commit(dq_full);
         }
+      umma_commit(acc_done);
     }
     __syncwarp();
+  } else if (warp >= 4) {
+    // ---------------- dQ reducer: thread = query row of the step ----------------
+    const int row = threadIdx.x - 128;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    bool ok = true;
+    int i = 0;
+    for (int ri = 0; ri < nr && ok; ++ri)
+      for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
+        ok = mbar_wait_warp(dq_full, i & 1);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t r0[32], r1[32];
+        tmem_ld32(tmem + lane_base + tDQ, r0);
+        tmem_ld32(tmem + lane_base + tDQ + 32, r1);
+        tc_fence_before();
+        mbar_arrive(dq_empty);
+        float* dst = p.dq_acc + (row0 + s + row) * 64;
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          red_add_v4(dst + 4 * c, __uint_as_float(r0[4 * c]), __uint_as_float(r0[4 * c + 1]),
+                     __uint_as_float(r0[4 * c + 2]), __uint_as_float(r0[4 * c + 3]));
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          red_add_v4(dst + 32 + 4 * c, __uint_as_float(r1[4 * c]), __uint_as_float(r1[4 * c + 1]),
+                     __uint_as_float(r1[4 * c + 2]), __uint_as_float(r1[4 * c + 3]));
+      }
   } else {
+    // ---------------- element-wise: thread = key row ----------------
+    const int row = threadIdx.x;
+    const int key = k_start + row;
     const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    const int row = threadIdx.x;  // query row within the step's tile
-    uint8_t* sP = smem + DkdvSmem::kP;
-    uint8_t* sDS = smem + DkdvSmem::kDS;
+    uint8_t* sDS = smem + BwdSmem::kDS;
     bool ok = true;
     int i = 0;
     for (int ri = 0; ri < nr && ok; ++ri) {
       const int rule = rg[ri].rule, shift = rg[ri].shift;
+      int qlo = -2147483647, qhi = 2147483647;  // visible query interval of this key
+      if (rule != 0)
+        dkdv_col_interval(rule, shift, key, rg[ri].lo < p.n ? 0 : p.n, p.n, p.bs, &qlo, &qhi);
       for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
-        const int qi = s + row;
-        const long long lrow = static_cast<long long>(bh) * 2 * p.n + qi;
-        const float L2 = p.lse[lrow] * 1.4426950408889634f;
-        const float Dl = p.delta[lrow];
-        int lo = -2147483647, hi = 2147483647;
-        if (rule != 0) {
-          train_row_interval(rule, shift, qi, p.n, p.bs, &lo, &hi);
-          lo -= k_start;
-          hi -= k_start;
-        }
-        ok = mbar_wait_warp(s_full, i & 1);
-        if (ok && i > 0) ok = mbar_wait_warp(mma_done, (i - 1) & 1);  // P/dS tiles are free
+        const int st = i % kBwdStages;
+        ok = mbar_wait_warp(&qd_full[st], (i / kBwdStages) & 1);  // L2 / Delta rows landed
+        if (ok) ok = mbar_wait_warp(s_full, i & 1);
         if (!ok) break;
         tc_fence_after();
+        const float* vL = reinterpret_cast<const float*>(smem + BwdSmem::kVec + st * 1024);
+        const float* vD = vL + 128;
+        const int lo = qlo - s, hi = qhi - s;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + c * 32, sr);
-          tmem_ld32(tmem + lane_base + 128 + c * 32, dr);
+          tmem_ld32(tmem + lane_base + tS + c * 32, sr);
+          tmem_ld32(tmem + lane_base + tDP + c * 32, dr);
           uint32_t pk[16], dk[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            float pv2[2], ds2[2];
+          for (int e4 = 0; e4 < 8; ++e4) {
+            const float4 l4 = *reinterpret_cast<const float4*>(vL + c * 32 + 4 * e4);
+            const float4 d4 = *reinterpret_cast<const float4*>(vD + c * 32 + 4 * e4);
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+            float pv[4], dsv[4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int col = c * 32 + 2 * e + h;
-              float pv = ex2(fmaf(__uint_as_float(sr[2 * e + h]), p.scale_log2, -L2));
-              if (rule != 0 && (col < lo || col >= hi)) pv = 0.f;
-              pv2[h] = pv;
-              ds2[h] = pv * (__uint_as_float(dr[2 * e + h]) - Dl);
+            for (int h = 0; h < 4; ++h) {
+              const int col = c * 32 + 4 * e4 + h;
+              float pe = ex2(fmaf(__uint_as_float(sr[4 * e4 + h]), p.scale_log2, -lv[h]));
+              if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
+              pv[h] = pe;
+              dsv[h] = pe * (__uint_as_float(dr[4 * e4 + h]) - dv4[h]);
             }
-            pk[e] = pack2<kBF16>(pv2[0], pv2[1]);
-            dk[e] = pack2<kBF16>(ds2[0], ds2[1]);
+            pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
+            pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
+            dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
+            dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
           }
-          // columns [32c, 32c+32) are 4 16-byte chunks of key half c/2
+          tmem_st16(tmem + lane_base + tS + c * 16, pk);
+          tmem_st16(tmem + lane_base + tDP + c * 16, dk);
+          // dS row for the dQ MMA: queries [32c, 32c+32) are 4 chunks of query half c/2
           const uint32_t half_off = (c >> 1) * kTile16;
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            const uint32_t off = half_off + sw128_offset(row, (c & 1) * 4 + ch);
-            *reinterpret_cast<uint4*>(sP + off) =
-                make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
-            *reinterpret_cast<uint4*>(sDS + off) =
+          for (int ch = 0; ch < 4; ++ch)
+            *reinterpret_cast<uint4*>(sDS + half_off + sw128_offset(row, (c & 1) * 4 + ch)) =
                 make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
-          }
         }
+        tmem_st_wait();
         fence_proxy_async_smem();
         tc_fence_before();
         mbar_arrive(p_full);
       }
     }
-    if (ok && i > 0) ok = mbar_wait_warp(mma_done, (i - 1) & 1);
-    ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+    if (ok) ok = mbar_wait_warp(acc_done, 0);
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-      const int key = k_start + row;  // accumulator lanes are keys
       uint8_t* dvp = reinterpret_cast<uint8_t*>(p.dv) +
                      2 * (bb * p.dv_sb + hh * p.dv_sh + static_cast<long long>(key) * p.dv_ss);
       uint8_t* dkp = reinterpret_cast<uint8_t*>(p.dk) +
                      2 * (bb * p.dk_sb + hh * p.dk_sh + static_cast<long long>(key) * p.dk_ss);
       if (i > 0) {
-        store_row64<kBF16>(tmem + lane_base + 256, dvp, 1.f);
-        store_row64<kBF16>(tmem + lane_base + 320, dkp, p.scale);
+        store_row64<kBF16>(tmem + lane_base + tDV, dvp, 1.f);
+        store_row64<kBF16>(tmem + lane_base + tDK, dkp, p.scale);
       } else {  // a key tile no query sees (cannot happen under the BD3-LM mask)
         uint4* a = reinterpret_cast<uint4*>(dvp);
         uint4* b = reinterpret_cast<uint4*>(dkp);
@@ -482,7 +404,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

@@ -296,7 +296,8 @@ int bd3_attn_fwd(const void* q, const void* k, const void* v, void* o, float* ls
 size_t bd3_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D) {
   (void)D;
   if (B < 1 || H < 1 || n < 1) return 0;
-  return static_cast<size_t>(B * H * 2 * n) * sizeof(float);
+  // Delta and LSE*log2(e) per query row, then the fp32 dQ accumulator (64 per row)
+  return static_cast<size_t>(B * H * 2 * n) * (1 + 1 + 64) * sizeof(float);
 }
 
 int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
@@ -315,7 +316,8 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 16)
     return fail(BD3_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,
                 workspace_bytes);
-  if (lse == nullptr) return fail(BD3_ERR_INVALID, "lse is required");
+  if (lse == nullptr || reinterpret_cast<uintptr_t>(lse) % 16)
+    return fail(BD3_ERR_INVALID, "lse must be a 16-byte aligned fp32 buffer");
   const int64_t S = 2 * n;
   CUtensorMap tq, tk, tv, tdo;
   if ((rc = make_map(&tq, q, dtype, S, H, B, strides + 0, 128, "q")) != BD3_OK) return rc;
@@ -330,11 +332,14 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
     if (reinterpret_cast<uintptr_t>(ptrs[t]) % 16 || s3[0] % 8 || s3[1] % 8 || s3[2] % 8)
       return fail(BD3_ERR_INVALID, "%s: pointer and strides must be 16-byte aligned", names[t]);
   }
+  const int64_t rows = B * H * S;
   bd3::BwdParams p{};
   p.o = o;
   p.dout = dout;
   p.lse = lse;
   p.delta = static_cast<float*>(workspace);
+  p.lse2 = p.delta + rows;
+  p.dq_acc = p.lse2 + rows;
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
@@ -346,34 +351,32 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   p.H = static_cast<int>(H);
   p.n = static_cast<int>(n);
   p.bs = static_cast<int>(block_size);
-  p.num_tiles = static_cast<int>(S / 128);
+  p.num_tiles = static_cast<int>(S / bd3::kBwdBKV);
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf = dtype == BD3_BF16;
-  const int64_t rows = B * H * S;
-  const unsigned dblocks = static_cast<unsigned>((rows * 8 + 255) / 256);
+  const unsigned eblocks = static_cast<unsigned>((rows * 8 + 255) / 256);
   {
     ProfScope ps(kPfDelta, st);
-    if (bf) bd3::bwd_delta_kernel<true><<<dblocks, 256, 0, st>>>(p, static_cast<int>(rows));
-    else bd3::bwd_delta_kernel<false><<<dblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    if (bf) bd3::bwd_prep_kernel<true><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    else bd3::bwd_prep_kernel<false><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
   }
-  if ((rc = check_launch("bwd_delta_kernel launch")) != BD3_OK) return rc;
+  if ((rc = check_launch("bwd_prep_kernel launch")) != BD3_OK) return rc;
   const unsigned grid = static_cast<unsigned>(B * H * p.num_tiles);
-  auto dqk = bf ? bd3::bwd_dq_kernel<true> : bd3::bwd_dq_kernel<false>;
-  if ((rc = set_smem(dqk, bd3::DqSmem::kAlloc, 4 + (bf ? 0 : 1))) != BD3_OK) return rc;
-  {
-    ProfScope ps(kPfDq, st);
-    dqk<<<grid, bd3::kBwdThreads, bd3::DqSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
-  }
-  if ((rc = check_launch("bwd_dq_kernel launch")) != BD3_OK) return rc;
-  auto dkv = bf ? bd3::bwd_dkdv_kernel<true> : bd3::bwd_dkdv_kernel<false>;
-  if ((rc = set_smem(dkv, bd3::DkdvSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
+  auto fused = bf ? bd3::bwd_fused_kernel<true> : bd3::bwd_fused_kernel<false>;
+  if ((rc = set_smem(fused, bd3::BwdSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
   {
     ProfScope ps(kPfDkdv, st);
-    dkv<<<grid, bd3::kBwdThreads, bd3::DkdvSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
+    fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
   }
-  return check_launch("bwd_dkdv_kernel launch");
+  if ((rc = check_launch("bwd_fused_kernel launch")) != BD3_OK) return rc;
+  {
+    ProfScope ps(kPfDq, st);
+    if (bf) bd3::bwd_dq_convert_kernel<true><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    else bd3::bwd_dq_convert_kernel<false><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+  }
+  return check_launch("bwd_dq_convert_kernel launch");
 }
 
 int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t block_size,
@@ -736,7 +739,7 @@ int bd3_debug_tiles(int32_t* out) {
   out[2] = bd3::kBwdBKV;
   out[3] = bd3::kBwdBQ;
   out[4] = bd3::kDecBN;
-  out[5] = bd3::kBwdDqBM;
+  out[5] = bd3::kBwdBQ;
   return 6;
 }
 

@@ -63,9 +63,12 @@ BD3_API int bd3_attn_fwd(const void* q, const void* k, const void* v, void* o, f
  * Replaces BlockSparseFlashAttention.backward (kernels/BlockSparseFlashAttention.py:509-562),
  * i.e. the host Delta = rowsum(dO * O) (:525) and the kernels
  * block_sparse_attention_bwd_dq_kern (:369-452) and block_sparse_attention_dk_dv_bwd_kern
- * (:213-328). dK and dV are deterministic (one program owns each key tile, no atomics).
+ * (:213-328), fused into one kernel per key tile. dK and dV are deterministic (one CTA owns
+ * each key tile and writes it once); dQ is summed in fp32 with atomic adds, so its last bits
+ * may vary from run to run.
  *   strides[24] = q, k, v, o, do, dq, dk, dv (batch, head, seq) in elements.
- *   workspace: bd3_attn_bwd_workspace_size() bytes of device memory (Delta scratch).
+ *   lse: 16-byte aligned. workspace: bd3_attn_bwd_workspace_size() bytes of device memory
+ *   (Delta, LSE*log2(e) and the fp32 dQ accumulator: 264 bytes per query row).
  * Requires n % 128 == 0 and n % block_size == 0 (the reference asserts both, :522, :548).
  */
 BD3_API size_t bd3_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D);
@@ -143,8 +146,9 @@ BD3_API int bd3_lse_merge(const float* parts, const float* lses, void* o, float*
 /* ---------------------------------------------------------------------------------------
  * Per-kernel timing for benchmarks. While enabled, every launch is bracketed by a pair of
  * CUDA events on its own stream (at most 8192 launches are kept). bd3_profile_collect()
- * waits for them and writes, per kernel id (0 training forward, 1 prefill forward, 2 Delta,
- * 3 dQ, 4 dK/dV, 5 decode, 6 decode combine), the summed milliseconds and launch counts to
+ * waits for them and writes, per kernel id (0 training forward, 1 prefill forward, 2 backward
+ * prep, 3 dQ convert, 4 fused backward, 5 decode, 6 decode combine), the summed milliseconds
+ * and launch counts to
  * total_ms[7] and counts[7]; it returns 7 and forgets the recorded launches.
  */
 BD3_API int bd3_profile_enable(int on);
@@ -155,7 +159,7 @@ BD3_API int bd3_profile_collect(double* total_ms, int32_t* counts);
  * bd3_debug_ranges: kind 0 forward/dQ key ranges, 1 dK/dV query ranges, 2 decode key ranges;
  * writes (lo, hi, rule, shift) quadruples to out[16]; returns how many.
  * bd3_debug_tiles: the library's tile sizes: out[0..5] = forward BM, BN; dK/dV BKV, BQ;
- * decode BN; dQ BM.
+ * decode BN; backward query step.
  */
 BD3_API int bd3_debug_ranges(int kind, int64_t start, int64_t tile_a, int64_t tile_b, int64_t n_or_qlen,
                      int64_t kv_len, int64_t block_size, int32_t* out);

@@ -52,9 +52,12 @@ def test_backward_matches_oracle(B, H, n, bs):
 
 
 def test_dkdv_deterministic():
+    """dK and dV are bitwise reproducible (one CTA owns each key tile and writes it once);
+    dQ is an fp32 atomic sum, equal up to summation order."""
     _, (_, dq1, dk1, dv1) = _run(2, 2, 256, 16, seed=5)
     _, (_, dq2, dk2, dv2) = _run(2, 2, 256, 16, seed=5)
-    assert torch.equal(dk1, dk2) and torch.equal(dv1, dv2) and torch.equal(dq1, dq2)
+    assert torch.equal(dk1, dk2) and torch.equal(dv1, dv2)
+    assert (dq1.float() - dq2.float()).abs().max().item() <= 1e-2
 
 
 @pytest.mark.parametrize("bs", [4, 16, 128])
