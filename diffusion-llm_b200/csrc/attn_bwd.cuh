@@ -308,8 +308,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (!ok) break;
         tc_fence_after();
         uint32_t r0[32], r1[32];
-        tmem_ld32(tmem + lane_base + tDQ, r0);
-        tmem_ld32(tmem + lane_base + tDQ + 32, r1);
+        tmem_ld32_async(tmem + lane_base + tDQ, r0);
+        tmem_ld32_async(tmem + lane_base + tDQ + 32, r1);
+        tmem_ld_wait();
+        reg_fence(r0);
+        reg_fence(r1);
         tc_fence_before();
         mbar_arrive(dq_empty);
         float* dst = p.dq_acc + (row0 + s + row) * 64;
@@ -344,11 +347,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const float* vL = reinterpret_cast<const float*>(smem + BwdSmem::kVec + st * 1024);
         const float* vD = vL + 128;
         const int lo = qlo - s, hi = qhi - s;
+        uint32_t sbuf[2][32], dbuf[2][32];
+        tmem_ld32_async(tmem + lane_base + tS, sbuf[0]);
+        tmem_ld32_async(tmem + lane_base + tDP, dbuf[0]);
+        tmem_ld_wait();
+        reg_fence(sbuf[0]);
+        reg_fence(dbuf[0]);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t sr[32], dr[32];
-          tmem_ld32(tmem + lane_base + tS + c * 32, sr);
-          tmem_ld32(tmem + lane_base + tDP + c * 32, dr);
+          uint32_t(&sr)[32] = sbuf[c & 1];
+          uint32_t(&dr)[32] = dbuf[c & 1];
+          if (c < 3) {  // next chunk's S and dP columns are read while this one is processed
+            tmem_ld32_async(tmem + lane_base + tS + (c + 1) * 32, sbuf[(c + 1) & 1]);
+            tmem_ld32_async(tmem + lane_base + tDP + (c + 1) * 32, dbuf[(c + 1) & 1]);
+          }
           uint32_t pk[16], dk[16];
 #pragma unroll
           for (int e4 = 0; e4 < 8; ++e4) {
@@ -377,6 +389,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           for (int ch = 0; ch < 4; ++ch)
             *reinterpret_cast<uint4*>(sDS + half_off + sw128_offset(row, (c & 1) * 4 + ch)) =
                 make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+          if (c < 3) {
+            tmem_ld_wait();
+            reg_fence(sbuf[(c + 1) & 1]);
+            reg_fence(dbuf[(c + 1) & 1]);
+          }
         }
         tmem_st_wait();
         fence_proxy_async_smem();

@@ -216,12 +216,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         if (!ok) break;
         tc_fence_after();
         float x[128];
+        {
+          uint32_t r[4][32];
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-          uint32_t r[32];
-          tmem_ld32(tmem + lane_base + b * 128 + c4 * 32, r);
+          for (int c4 = 0; c4 < 4; ++c4) tmem_ld32_async(tmem + lane_base + b * 128 + c4 * 32, r[c4]);
+          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = __uint_as_float(r[i]);
+          for (int c4 = 0; c4 < 4; ++c4) {
+            reg_fence(r[c4]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) x[c4 * 32 + i] = __uint_as_float(r[c4][i]);
+          }
         }
         if (rule != 0) {
           const int lo = vlo - s, hi = vhi - s;
@@ -266,13 +271,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         // the rescale's TMEM load/store is warp-collective: vote, and let the rows that do not
         // need it multiply by alpha = 1
         if (__any_sync(0xffffffffu, rescale)) {
+          uint32_t r[2][32];
+          tmem_ld32_async(tmem + lane_base + 256, r[0]);
+          tmem_ld32_async(tmem + lane_base + 256 + 32, r[1]);
+          tmem_ld_wait();
 #pragma unroll
           for (int c2 = 0; c2 < 2; ++c2) {
-            uint32_t r[32];
-            tmem_ld32(tmem + lane_base + 256 + c2 * 32, r);
+            reg_fence(r[c2]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tmem + lane_base + 256 + c2 * 32, r);
+            for (int i = 0; i < 32; ++i)
+              r[c2][i] = __float_as_uint(__uint_as_float(r[c2][i]) * alpha);
+            tmem_st32(tmem + lane_base + 256 + c2 * 32, r[c2]);
           }
           tmem_st_wait();
         }
