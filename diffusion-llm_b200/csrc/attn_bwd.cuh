@@ -18,15 +18,19 @@
 //                       warpgroup with vector reductions (red.global.add.v4.f32).
 //   bwd_dq_convert_kernel  dQ = scale * accumulator, in the input dtype.
 //
-// Roles in the fused kernel (320 threads):
-//   warps 0-3  element-wise: thread t owns key row t of the tile (TMEM lane t)
-//   warps 4-7  dQ reducer: thread t owns query row t of dQ_i (TMEM lane t)
-//   warp 8     TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
-//   warp 9     TMEM owner and UMMA issuer
-// TMEM columns: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ_i [384,448);
-// P^T (packed 16-bit) overwrites S^T [0,64) and dS^T overwrites dP^T [128,192).
-// dS for the dQ MMA lives in shared memory as [query half][key row][64 queries] with the
-// 128-byte swizzle, which is the MN-major A operand (M = queries, K = keys).
+// Each 128-query step runs as two 64-query halves whose S^T/dP^T live in two TMEM buffers, so
+// the MMAs of one half overlap the element-wise pass over the other.
+// Roles in the fused kernel (448 threads):
+//   warps 0-7  element-wise: two warpgroups; thread t of each owns key row t (TMEM lane t),
+//              warpgroup g takes queries [32g, 32g+32) of every half-step
+//   warps 8-11 dQ reducer: thread t owns query row t of dQ_i (TMEM lane t)
+//   warp 12    TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
+//   warp 13    TMEM owner and UMMA issuer
+// TMEM columns: half-step buffers [0,128) and [128,256) (S^T then dP^T, 64 columns each),
+// dV [256,320), dK [320,384), dQ_i [384,448). P^T and dS^T (packed 16-bit) overwrite the
+// columns each thread has already read. dS for the dQ MMA lives in shared memory (two
+// buffers) as [query half][key row][64 queries] with the 128-byte swizzle: the MN-major A
+// operand of dQ_i = dS_i K (M = 128 queries, K = 128 keys).
 #pragma once
 
 #include "attn_fwd.cuh"
@@ -38,7 +42,7 @@ namespace bd3 {
 constexpr int kBwdBKV = 128;  // keys per CTA
 constexpr int kBwdBQ = 128;   // queries per step
 constexpr int kBwdStages = 2;
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 448;
 
 struct BwdParams {
   const void* o;
@@ -148,11 +152,12 @@ struct BwdSmem {
   static constexpr uint32_t kV = kK + kTile16;
   static constexpr uint32_t kQ = kV + kTile16;                  // [stage]
   static constexpr uint32_t kDO = kQ + kBwdStages * kTile16;    // [stage]
-  static constexpr uint32_t kDS = kDO + kBwdStages * kTile16;   // [query half][128 keys][128 B]
-  static constexpr uint32_t kVec = kDS + 2 * kTile16;           // [stage][L2 128 | Delta 128]
+  static constexpr uint32_t kDS = kDO + kBwdStages * kTile16;   // [buffer][q half][key][128 B]
+  static constexpr uint32_t kVec = kDS + 2 * 2 * kTile16;       // [stage][L2 128 | Delta 128]
   static constexpr uint32_t kBar = kVec + kBwdStages * 1024;
-  // kv_full, qd_full[S], qd_empty[S], s_full, p_full, dq_full, dq_empty, acc_done
-  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 5;
+  // kv_full, qd_full[S], qd_empty[S], s_full[2], p_full[2], ds_free[2], dq_full, dq_empty,
+  // acc_done
+  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 6 + 3;
   static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
   static constexpr uint32_t kAlloc = kTmemSlot + 16 + 1024;
 };
@@ -165,6 +170,11 @@ __device__ __forceinline__ int bwd_tile_order(int t, int num_tiles) {
   return t - half;
 }
 
+// Column of the packed 16-bit P^T / dS^T operand for k-step kk (16 queries) of a half-step:
+// element-wise warpgroup g writes queries [32g, 32g+32) of the half into its own 32 read
+// columns, so queries [0,32) sit at columns [0,16) and [32,64) at [32,48).
+__device__ __forceinline__ uint32_t half_ts_col(int kk) { return kk < 2 ? kk * 8 : 32 + (kk - 2) * 8; }
+
 template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -176,11 +186,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* kv_full = bars;
   uint64_t* qd_full = bars + 1;
   uint64_t* qd_empty = bars + 1 + kBwdStages;
-  uint64_t* s_full = bars + 1 + 2 * kBwdStages;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* dq_full = s_full + 2;
-  uint64_t* dq_empty = s_full + 3;
-  uint64_t* acc_done = s_full + 4;
+  uint64_t* s_full = bars + 1 + 2 * kBwdStages;  // [half]
+  uint64_t* p_full = s_full + 2;                  // [half]
+  uint64_t* ds_free = s_full + 4;                 // [dS buffer]
+  uint64_t* dq_full = s_full + 6;
+  uint64_t* dq_empty = s_full + 7;
+  uint64_t* acc_done = s_full + 8;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BwdSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
@@ -199,14 +210,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&qd_full[s], 1);
       mbar_init(&qd_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
+    for (int h = 0; h < 2; ++h) {
+      mbar_init(&s_full[h], 1);
+      mbar_init(&p_full[h], 256);
+      mbar_init(&ds_free[h], 1);
+    }
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(acc_done, 1);
     fence_mbar_init();
   }
-  if (warp == 9) {
+  if (warp == 13) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -214,9 +228,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  constexpr uint32_t tS = 0, tDP = 128, tDV = 256, tDK = 320, tDQ = 384;
+  // TMEM columns: half-step buffer h at [128h, 128h+128) = S^T [0,64) then dP^T [64,128);
+  // dV [256,320), dK [320,384), dQ [384,448)
+  constexpr uint32_t tDV = 256, tDK = 320, tDQ = 384;
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ---------------- TMA producer ----------------
     if (elect_one()) {
       bool ok = true;
@@ -238,18 +254,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         }
     }
     __syncwarp();
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ---------------- UMMA issuer ----------------
     if (elect_one()) {
-      constexpr uint32_t idesc_s = idesc_f16(128, 128, false, false, kBF16);
+      constexpr uint32_t idesc_s = idesc_f16(128, 64, false, false, kBF16);
       constexpr uint32_t idesc_ts = idesc_f16(128, 64, false, true, kBF16);
       constexpr uint32_t idesc_dq = idesc_f16(128, 64, true, true, kBF16);
       const uint32_t sbase = smem_u32(smem);
       const uint64_t kdesc = sw128_desc(sbase + BwdSmem::kK, 16, 1024);
       const uint64_t vdesc = sw128_desc(sbase + BwdSmem::kV, 16, 1024);
       const uint64_t kmn = sw128_desc(sbase + BwdSmem::kK, kTile16, 1024);
-      const uint64_t dsdesc = sw128_desc(sbase + BwdSmem::kDS, kTile16, 1024);
       bool ok = mbar_wait(kv_full, 0);
+      // dV/dK of half-step jp (and, when it completes a step, that step's dQ)
+      auto finish = [&](int jp) {
+        const int hp = jp & 1, ip = jp >> 1, stp = ip % kBwdStages;
+        ok = ok && mbar_wait(&p_full[hp], ip & 1);
+        if (!ok) return;
+        tc_fence_after();
+        const uint32_t qa = sbase + BwdSmem::kQ + stp * kTile16 + hp * (kTile16 / 2);
+        const uint32_t da = sbase + BwdSmem::kDO + stp * kTile16 + hp * (kTile16 / 2);
+        const uint64_t domn = sw128_desc(da, kTile16, 1024);
+        const uint64_t qmn = sw128_desc(qa, kTile16, 1024);
+        const uint32_t tbuf = tmem + hp * 128;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_ts(tmem + tDV, tbuf + half_ts_col(kk), domn + ((kk * 2048) >> 4), idesc_ts,
+                  (jp > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_ts(tmem + tDK, tbuf + 64 + half_ts_col(kk), qmn + ((kk * 2048) >> 4), idesc_ts,
+                  (jp > 0 || kk > 0) ? 1u : 0u);
+        if (hp == 1) {  // step ip is complete: its Q/dO stage is free, and dQ can run
+          umma_commit(&qd_empty[stp]);
+          if (ip > 0) {
+            ok = mbar_wait(dq_empty, (ip - 1) & 1);  // the reducer has read dQ_{ip-1}
+            if (!ok) return;
+            tc_fence_after();
+          }
+          const uint64_t dsdesc =
+              sw128_desc(sbase + BwdSmem::kDS + (ip & 1) * 2 * kTile16, kTile16, 1024);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            umma_ss(tmem + tDQ, dsdesc + ((kk * 2048) >> 4), kmn + ((kk * 2048) >> 4),
+                    idesc_dq, kk > 0 ? 1u : 0u);
+          umma_commit(dq_full);
+          umma_commit(&ds_free[ip & 1]);
+        }
+      };
+      int j = 0;
       int i = 0;
       for (int ri = 0; ri < nr && ok; ++ri)
         for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdBQ, ++i) {
@@ -257,48 +309,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = mbar_wait(&qd_full[st], (i / kBwdStages) & 1);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t qa = sbase + BwdSmem::kQ + st * kTile16;
-          const uint32_t da = sbase + BwdSmem::kDO + st * kTile16;
-          const uint64_t qdesc = sw128_desc(qa, 16, 1024);
-          const uint64_t dodesc = sw128_desc(da, 16, 1024);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + tS, kdesc + kk * 2, qdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+          for (int h = 0; h < 2; ++h, ++j) {
+            const uint32_t qa = sbase + BwdSmem::kQ + st * kTile16 + h * (kTile16 / 2);
+            const uint32_t da = sbase + BwdSmem::kDO + st * kTile16 + h * (kTile16 / 2);
+            const uint64_t qdesc = sw128_desc(qa, 16, 1024);
+            const uint64_t dodesc = sw128_desc(da, 16, 1024);
+            const uint32_t tbuf = tmem + h * 128;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + tDP, vdesc + kk * 2, dodesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
-          umma_commit(s_full);
-          ok = mbar_wait(p_full, i & 1);
-          if (!ok) break;
-          tc_fence_after();
-          const uint64_t domn = sw128_desc(da, kTile16, 1024);
-          const uint64_t qmn = sw128_desc(qa, kTile16, 1024);
+            for (int kk = 0; kk < 4; ++kk)
+              umma_ss(tbuf, kdesc + kk * 2, qdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_ts(tmem + tDV, tmem + tS + kk * 8, domn + ((kk * 2048) >> 4), idesc_ts,
-                    (i > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_ts(tmem + tDK, tmem + tDP + kk * 8, qmn + ((kk * 2048) >> 4), idesc_ts,
-                    (i > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&qd_empty[st]);
-          if (i > 0) {
-            ok = mbar_wait(dq_empty, (i - 1) & 1);  // the reducer has read dQ_{i-1}
+            for (int kk = 0; kk < 4; ++kk)
+              umma_ss(tbuf + 64, vdesc + kk * 2, dodesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+            umma_commit(&s_full[h]);
+            if (j > 0) finish(j - 1);
             if (!ok) break;
-            tc_fence_after();
           }
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_ss(tmem + tDQ, dsdesc + ((kk * 2048) >> 4), kmn + ((kk * 2048) >> 4), idesc_dq,
-                    kk > 0 ? 1u : 0u);
-          umma_commit(dq_full);
         }
+      if (ok && j > 0) finish(j - 1);
       umma_commit(acc_done);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  } else if (warp >= 8) {
     // ---------------- dQ reducer: thread = query row of the step ----------------
-    const int row = threadIdx.x - 128;
+    const int row = threadIdx.x - 256;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
     int i = 0;
@@ -326,11 +361,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                      __uint_as_float(r1[4 * c + 2]), __uint_as_float(r1[4 * c + 3]));
       }
   } else {
-    // ---------------- element-wise: thread = key row ----------------
-    const int row = threadIdx.x;
+    // ------- element-wise: thread = key row; warpgroup g takes queries [32g, 32g+32) of
+    // each 64-query half-step -------
+    const int g = warp >> 2;
+    const int row = threadIdx.x & 127;
     const int key = k_start + row;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
-    uint8_t* sDS = smem + BwdSmem::kDS;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
     int i = 0;
     for (int ri = 0; ri < nr && ok; ++ri) {
@@ -341,87 +377,79 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
         const int st = i % kBwdStages;
         ok = mbar_wait_warp(&qd_full[st], (i / kBwdStages) & 1);  // L2 / Delta rows landed
-        if (ok) ok = mbar_wait_warp(s_full, i & 1);
+        if (ok && i >= 2) ok = mbar_wait_warp(&ds_free[i & 1], ((i >> 1) - 1) & 1);
         if (!ok) break;
-        tc_fence_after();
         const float* vL = reinterpret_cast<const float*>(smem + BwdSmem::kVec + st * 1024);
         const float* vD = vL + 128;
-        const int lo = qlo - s, hi = qhi - s;
-        uint32_t sbuf[2][32], dbuf[2][32];
-        tmem_ld32_async(tmem + lane_base + tS, sbuf[0]);
-        tmem_ld32_async(tmem + lane_base + tDP, dbuf[0]);
-        tmem_ld_wait();
-        reg_fence(sbuf[0]);
-        reg_fence(dbuf[0]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t(&sr)[32] = sbuf[c & 1];
-          uint32_t(&dr)[32] = dbuf[c & 1];
-          if (c < 3) {  // next chunk's S and dP columns are read while this one is processed
-            tmem_ld32_async(tmem + lane_base + tS + (c + 1) * 32, sbuf[(c + 1) & 1]);
-            tmem_ld32_async(tmem + lane_base + tDP + (c + 1) * 32, dbuf[(c + 1) & 1]);
-          }
+        uint8_t* sDS = smem + BwdSmem::kDS + (i & 1) * 2 * kTile16;
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          ok = mbar_wait_warp(&s_full[h], i & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t tbuf = tmem + lane_base + h * 128 + g * 32;
+          uint32_t sr[32], dr[32];
+          tmem_ld32_async(tbuf, sr);
+          tmem_ld32_async(tbuf + 64, dr);
+          tmem_ld_wait();
+          reg_fence(sr);
+          reg_fence(dr);
+          const int c0 = h * 64 + g * 32;  // first query of this thread's columns, in the step
+          const int lo = qlo - s - c0, hi = qhi - s - c0;
           uint32_t pk[16], dk[16];
 #pragma unroll
           for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(vL + c * 32 + 4 * e4);
-            const float4 d4 = *reinterpret_cast<const float4*>(vD + c * 32 + 4 * e4);
+            const float4 l4 = *reinterpret_cast<const float4*>(vL + c0 + 4 * e4);
+            const float4 d4 = *reinterpret_cast<const float4*>(vD + c0 + 4 * e4);
             const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
             float pv[4], dsv[4];
 #pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const int col = c * 32 + 4 * e4 + h;
-              float pe = ex2(fmaf(__uint_as_float(sr[4 * e4 + h]), p.scale_log2, -lv[h]));
+            for (int e = 0; e < 4; ++e) {
+              const int col = 4 * e4 + e;
+              float pe = ex2(fmaf(__uint_as_float(sr[col]), p.scale_log2, -lv[e]));
               if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
-              pv[h] = pe;
-              dsv[h] = pe * (__uint_as_float(dr[4 * e4 + h]) - dv4[h]);
+              pv[e] = pe;
+              dsv[e] = pe * (__uint_as_float(dr[col]) - dv4[e]);
             }
             pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
             pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
             dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
             dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
           }
-          tmem_st16(tmem + lane_base + tS + c * 16, pk);
-          tmem_st16(tmem + lane_base + tDP + c * 16, dk);
-          // dS row for the dQ MMA: queries [32c, 32c+32) are 4 chunks of query half c/2
-          const uint32_t half_off = (c >> 1) * kTile16;
+          tmem_st16(tbuf, pk);        // P^T over this thread's own (already read) S^T columns
+          tmem_st16(tbuf + 64, dk);   // dS^T likewise over dP^T
+          // dS row for the dQ MMA: queries [32g, 32g+32) of half h are 16-byte chunks 4g..4g+3
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch)
-            *reinterpret_cast<uint4*>(sDS + half_off + sw128_offset(row, (c & 1) * 4 + ch)) =
+            *reinterpret_cast<uint4*>(sDS + h * kTile16 + sw128_offset(row, 4 * g + ch)) =
                 make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
-          if (c < 3) {
-            tmem_ld_wait();
-            reg_fence(sbuf[(c + 1) & 1]);
-            reg_fence(dbuf[(c + 1) & 1]);
-          }
+          tmem_st_wait();
+          fence_proxy_async_smem();
+          tc_fence_before();
+          mbar_arrive(&p_full[h]);
         }
-        tmem_st_wait();
-        fence_proxy_async_smem();
-        tc_fence_before();
-        mbar_arrive(p_full);
       }
     }
     if (ok) ok = mbar_wait_warp(acc_done, 0);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
-      uint8_t* dvp = reinterpret_cast<uint8_t*>(p.dv) +
-                     2 * (bb * p.dv_sb + hh * p.dv_sh + static_cast<long long>(key) * p.dv_ss);
-      uint8_t* dkp = reinterpret_cast<uint8_t*>(p.dk) +
-                     2 * (bb * p.dk_sb + hh * p.dk_sh + static_cast<long long>(key) * p.dk_ss);
+      // warpgroup 0 writes dV, warpgroup 1 writes dK (accumulator lanes are keys)
+      uint8_t* dst = g == 0 ? reinterpret_cast<uint8_t*>(p.dv) +
+                                  2 * (bb * p.dv_sb + hh * p.dv_sh + static_cast<long long>(key) * p.dv_ss)
+                            : reinterpret_cast<uint8_t*>(p.dk) +
+                                  2 * (bb * p.dk_sb + hh * p.dk_sh + static_cast<long long>(key) * p.dk_ss);
       if (i > 0) {
-        store_row64<kBF16>(tmem + lane_base + tDV, dvp, 1.f);
-        store_row64<kBF16>(tmem + lane_base + tDK, dkp, p.scale);
+        store_row64<kBF16>(tmem + lane_base + (g == 0 ? tDV : tDK), dst, g == 0 ? 1.f : p.scale);
       } else {  // a key tile no query sees (cannot happen under the BD3-LM mask)
-        uint4* a = reinterpret_cast<uint4*>(dvp);
-        uint4* b = reinterpret_cast<uint4*>(dkp);
-        for (int t = 0; t < 8; ++t) a[t] = b[t] = make_uint4(0, 0, 0, 0);
+        uint4* a = reinterpret_cast<uint4*>(dst);
+        for (int t = 0; t < 8; ++t) a[t] = make_uint4(0, 0, 0, 0);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == 13) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
