@@ -15,7 +15,7 @@
 //                         dQ_i = dS_i K                              (SS MMA from a smem dS tile)
 //                       dV and dK accumulate in TMEM and are written once, so they are
 //                       deterministic; each dQ_i is added to the fp32 accumulator by a reducer
-//                       warpgroup with vector reductions (red.global.add.v4.f32).
+//                       warpgroup through TMA reduce-adds (cp.reduce.async.bulk.tensor).
 //   bwd_dq_convert_kernel  dQ = scale * accumulator, in the input dtype.
 //
 // Each 128-query step runs as two 64-query halves whose S^T/dP^T live in two TMEM buffers, so
@@ -23,7 +23,8 @@
 // Roles in the fused kernel (448 threads):
 //   warps 0-7  element-wise: two warpgroups; thread t of each owns key row t (TMEM lane t),
 //              warpgroup g takes queries [32g, 32g+32) of every half-step
-//   warps 8-11 dQ reducer: thread t owns query row t of dQ_i (TMEM lane t)
+//   warps 8-11 dQ reducer: thread t owns query row t of dQ_i (TMEM lane t); stages dQ_i in
+//              shared memory and adds it to the fp32 accumulator with TMA reduce-adds
 //   warp 12    TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
 //   warp 13    TMEM owner and UMMA issuer
 // TMEM columns: half-step buffers [0,128) and [128,256) (S^T then dP^T, 64 columns each),
@@ -65,6 +66,28 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
                "f"(c), "f"(d)
                : "memory");
+}
+
+// Tiled TMA reduce-add of a shared-memory box into global memory (fp32 add in L2), tracked by
+// the issuing thread's bulk async-group.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* src, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// Wait until every committed bulk group has finished reading its shared-memory source.
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// Wait until every committed bulk group has completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size % 16 == 0).
@@ -154,7 +177,8 @@ struct BwdSmem {
   static constexpr uint32_t kDO = kQ + kBwdStages * kTile16;    // [stage]
   static constexpr uint32_t kDS = kDO + kBwdStages * kTile16;   // [buffer][q half][key][128 B]
   static constexpr uint32_t kVec = kDS + 2 * 2 * kTile16;       // [stage][L2 128 | Delta 128]
-  static constexpr uint32_t kBar = kVec + kBwdStages * 1024;
+  static constexpr uint32_t kRed = kVec + kBwdStages * 1024;    // dQ_i staging: [2 boxes][128][128 B]
+  static constexpr uint32_t kBar = kRed + 2 * kTile16;
   // kv_full, qd_full[S], qd_empty[S], s_full[2], p_full[2], ds_free[2], dq_full, dq_empty,
   // acc_done
   static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 6 + 3;
@@ -179,7 +203,7 @@ template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const BwdParams p) {
+                     const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BwdSmem::kBar);
@@ -333,13 +357,29 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     __syncwarp();
   } else if (warp >= 8) {
     // ---------------- dQ reducer: thread = query row of the step ----------------
+    // dQ_i goes from TMEM to a swizzled shared-memory tile (two 32-column boxes) and from
+    // there into the fp32 accumulator by two TMA reduce-adds, so the additions run in L2
+    // without occupying this SM's load/store path.
     const int row = threadIdx.x - 256;
+    const bool leader = (threadIdx.x == 256);
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint8_t* stage = smem + BwdSmem::kRed;
     bool ok = true;
     int i = 0;
     for (int ri = 0; ri < nr && ok; ++ri)
       for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
         ok = mbar_wait_warp(dq_full, i & 1);
+        // the four reducer warps share named barriers below: agree on leaving the loop
+        {
+          uint32_t all;
+          asm volatile(
+              "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 2, 128, p;\n"
+              " selp.u32 %0, 1, 0, q;\n}\n"
+              : "=r"(all)
+              : "r"(static_cast<uint32_t>(ok))
+              : "memory");
+          ok = all != 0;
+        }
         if (!ok) break;
         tc_fence_after();
         uint32_t r0[32], r1[32];
@@ -350,16 +390,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         reg_fence(r1);
         tc_fence_before();
         mbar_arrive(dq_empty);
-        float* dst = p.dq_acc + (row0 + s + row) * 64;
+        if (leader) bulk_wait_group_read0();  // the previous reduce has read the staging tile
+        asm volatile("bar.sync 2, 128;" ::: "memory");
 #pragma unroll
-        for (int c = 0; c < 8; ++c)
-          red_add_v4(dst + 4 * c, __uint_as_float(r0[4 * c]), __uint_as_float(r0[4 * c + 1]),
-                     __uint_as_float(r0[4 * c + 2]), __uint_as_float(r0[4 * c + 3]));
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          red_add_v4(dst + 32 + 4 * c, __uint_as_float(r1[4 * c]), __uint_as_float(r1[4 * c + 1]),
-                     __uint_as_float(r1[4 * c + 2]), __uint_as_float(r1[4 * c + 3]));
+        for (int c = 0; c < 8; ++c) {
+          *reinterpret_cast<uint4*>(stage + sw128_offset(row, c)) =
+              make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
+          *reinterpret_cast<uint4*>(stage + kTile16 + sw128_offset(row, c)) =
+              make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (leader) {
+          const int y = static_cast<int>(row0 + s);
+          tma_reduce_add_2d(&tm_dqacc, stage, 0, y);
+          tma_reduce_add_2d(&tm_dqacc, stage + kTile16, 32, y);
+          bulk_commit_group();
+        }
       }
+    if (leader) bulk_wait_group0();  // every reduce has landed before the CTA exits
   } else {
     // ------- element-wise: thread = key row; warpgroup g takes queries [32g, 32g+32) of
     // each 64-query half-step -------

@@ -333,6 +333,21 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
       return fail(BD3_ERR_INVALID, "%s: pointer and strides must be 16-byte aligned", names[t]);
   }
   const int64_t rows = B * H * S;
+  // the fp32 dQ accumulator as a (rows, 64) matrix for the TMA reduce-adds: 32-column boxes
+  // of 128 rows with the 128-byte swizzle
+  CUtensorMap tdqa;
+  {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return fail(BD3_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    float* acc = static_cast<float*>(workspace) + 2 * rows;
+    cuuint64_t dims[2] = {64, static_cast<cuuint64_t>(rows)};
+    cuuint64_t gstr[1] = {64 * sizeof(float)};
+    cuuint32_t box[2] = {32, 128}, estr[2] = {1, 1};
+    const CUresult r = fn(&tdqa, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, acc, dims, gstr, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(BD3_ERR_CUDA, "dQ accumulator tensor map failed (%d)", int(r));
+  }
   bd3::BwdParams p{};
   p.o = o;
   p.dout = dout;
@@ -368,7 +383,7 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   if ((rc = set_smem(fused, bd3::BwdSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
   {
     ProfScope ps(kPfDkdv, st);
-    fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, p);
+    fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, tdqa, p);
   }
   if ((rc = check_launch("bwd_fused_kernel launch")) != BD3_OK) return rc;
   {
