@@ -209,10 +209,8 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   p.kv_len = static_cast<int>(kv_len);
   p.bs = static_cast<int>(bs);
   p.num_q_tiles = static_cast<int>(bd3::cdiv(static_cast<int>(q_rows), bd3::kFwdBM));
-  // training pairs noisy tile i with clean tile i; prefill pairs tiles 2p and 2p+1
-  p.num_pairs = mode == bd3::kTrain ? p.num_q_tiles / 2 : bd3::cdiv(p.num_q_tiles, 2);
   p.scale_log2 = 0.125f * 1.4426950408889634f;
-  const int64_t grid = B * H * p.num_pairs;
+  const int64_t grid = B * H * p.num_q_tiles;
   if (grid > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "grid too large");
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const bd3::FwdParams);
   int slot;
