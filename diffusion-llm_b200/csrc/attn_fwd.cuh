@@ -4,16 +4,18 @@
 // the training layout, and block_sparse_decode_kern (kernels/BlockSparseDecodeAttention.py:
 // 41-110) for prefill-sized decode calls (q_len > 64).
 //
-// One CTA per (batch*head, 128-row query tile); key tiles of 128, visited heaviest tile first.
-// S = Q K_j^T is double-buffered in TMEM, so the tensor cores compute tile j+1 while the
-// softmax works on tile j. The softmax is split by key columns between two warpgroups: each
-// owns 64 of every tile's 128 keys for all 128 rows and keeps its own running max, row sum
+// Persistent: one CTA per SM steps through (batch*head, 128-row query tile) work items,
+// heaviest tiles first, with TMEM, barriers and the K/V ring kept across items and the Q tile
+// double-buffered, so one item's prologue and epilogue overlap its neighbours' work. Key
+// tiles are 128 wide. S = Q K_j^T is double-buffered in TMEM, so the tensor cores compute
+// tile j+1 while the softmax works on tile j. The softmax is split by key columns between
+// two warpgroups: each owns 64 of every tile's 128 keys for all 128 rows and keeps its own running max, row sum
 // and O accumulator (an in-CTA split of the keys), and the two halves are merged once at the
 // end with the split-KV weighting. No per-tile exchange between the warpgroups is needed.
 // Roles (320 threads):
 //   warps 0-3  softmax, key columns [0,64) of every tile: thread t owns query row t (TMEM lane t)
 //   warps 4-7  softmax, key columns [64,128)
-//   warp 8     TMA producer: Q once, then K and V tiles into a kFwdStages-deep ring
+//   warp 8     TMA producer: each item's Q tile, then its K and V tiles into the ring
 //   warp 9     TMEM owner and UMMA issuer (one thread):
 //              S[j&1] = Q K_j^T (SS, M=128 N=128 K=64), then for each half g
 //              O_g += P_g V_j[64g, 64g+64) (TS: P_g from TMEM, V an MN-major smem operand)
@@ -49,18 +51,20 @@ struct FwdParams {
   int q_len, kv_len;     // decode: rows and keys per (batch, head)
   int bs;                // block size
   int num_q_tiles;       // query tiles per (batch, head)
+  int num_bh;            // batch * heads
   float scale_log2;      // softmax scale * log2(e)
 };
 
 struct FwdSmem {
-  static constexpr uint32_t kQ = 0;
-  static constexpr uint32_t kK = kQ + kTile16;
+  static constexpr uint32_t kQ = 0;                          // [item parity]
+  static constexpr uint32_t kK = kQ + 2 * kTile16;
   static constexpr uint32_t kV = kK + kFwdStages * kTile16;
   static constexpr uint32_t kBar = kV + kFwdStages * kTile16;
-  // q_full, k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2], o_done[2]
-  static constexpr uint32_t kNumBars = 1 + 3 * kFwdStages + 6;
-  static constexpr uint32_t kMerge = kBar + kNumBars * 8;    // warpgroup 1's (m, l) per row
-  static constexpr uint32_t kTmemSlot = kMerge + 2 * 128 * 4;
+  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
+  // o_done[2], o_free
+  static constexpr uint32_t kNumBars = 4 + 3 * kFwdStages + 7;
+  static constexpr uint32_t kMerge = kBar + kNumBars * 8;    // [item parity] warpgroup 1's m, l
+  static constexpr uint32_t kTmemSlot = kMerge + 2 * 2 * 128 * 4;
   static constexpr uint32_t kBytes = kTmemSlot + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // room to align the base to 1 KB
 };
@@ -82,6 +86,20 @@ __device__ __forceinline__ int fwd_make_ranges(const FwdParams& p, int q_start, 
   return decode_ranges(q_start, kFwdBM, kFwdBN, p.q_len, p.kv_len, p.bs, r);
 }
 
+// Decode work item w of the persistent loop: its (batch*head) and query tile.
+__device__ __forceinline__ void fwd_item(int w, const FwdParams& p, int mode, int* bh,
+                                         int* q_tile) {
+  *bh = w % p.num_bh;
+  *q_tile = fwd_tile_order(w / p.num_bh, p.num_q_tiles, mode);
+}
+
+__device__ __forceinline__ int fwd_count_tiles(const Range* r, int nr) {
+  int c = 0;
+  for (int i = 0; i < nr; ++i)
+    if (r[i].hi > r[i].lo) c += cdiv(r[i].hi - r[i].lo, kFwdBN);
+  return c;
+}
+
 template <int kMode, bool kBF16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -91,29 +109,25 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FwdSmem::kBar);
-  uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;
-  uint64_t* v_full = bars + 1 + kFwdStages;
-  uint64_t* kv_empty = bars + 1 + 2 * kFwdStages;
-  uint64_t* s_full = bars + 1 + 3 * kFwdStages;  // [buffer]
+  uint64_t* q_full = bars;                        // [item parity]
+  uint64_t* q_empty = bars + 2;                   // [item parity]
+  uint64_t* k_full = bars + 4;
+  uint64_t* v_full = bars + 4 + kFwdStages;
+  uint64_t* kv_empty = bars + 4 + 2 * kFwdStages;
+  uint64_t* s_full = bars + 4 + 3 * kFwdStages;  // [buffer]
   uint64_t* p_full = s_full + 2;                  // [warpgroup]
   uint64_t* o_done = s_full + 4;                  // [warpgroup]
-  float* merge_m = reinterpret_cast<float*>(smem + FwdSmem::kMerge);
-  float* merge_l = merge_m + 128;
+  uint64_t* o_free = s_full + 6;                  // the epilogue has read O_0 and O_1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + FwdSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
-  const int BH = gridDim.x / p.num_q_tiles;
-  const int bh = blockIdx.x % BH;
-  const int q_tile = fwd_tile_order(blockIdx.x / BH, p.num_q_tiles, kMode);
-  const int q_start = q_tile * kFwdBM;
-  const int bb = bh / p.H, hh = bh % p.H;
-
-  Range rg[3];
-  const int nr = fwd_make_ranges<kMode>(p, q_start, rg);
+  const int num_items = p.num_bh * p.num_q_tiles;
 
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     for (int s = 0; s < kFwdStages; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
@@ -124,6 +138,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       mbar_init(&p_full[g], 128);
       mbar_init(&o_done[g], 1);
     }
+    mbar_init(o_free, 128);
     fence_mbar_init();
   }
   if (warp == 9) {
@@ -144,18 +159,28 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     // ---------------- TMA producer ----------------
     if (elect_one()) {
       bool ok = true;
-      mbar_expect_tx(q_full, kTile16);
-      tma_load_4d(&tm_q, q_full, smem + FwdSmem::kQ, 0, q_start, hh, bb);
-      int j = 0;
-      for (int ri = 0; ri < nr && ok; ++ri) {
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kFwdBN, ++j) {
-          const int st = j % kFwdStages;
-          if (j >= kFwdStages) ok = mbar_wait(&kv_empty[st], ((j / kFwdStages) - 1) & 1);
-          if (!ok) break;
-          mbar_expect_tx(&k_full[st], kTile16);
-          tma_load_4d(&tm_k, &k_full[st], smem + FwdSmem::kK + st * kTile16, 0, s, hh, bb);
-          mbar_expect_tx(&v_full[st], kTile16);
-          tma_load_4d(&tm_v, &v_full[st], smem + FwdSmem::kV + st * kTile16, 0, s, hh, bb);
+      int J = 0;  // key tiles loaded so far by this CTA
+      for (int w = blockIdx.x, it = 0; w < num_items && ok; w += gridDim.x, ++it) {
+        int bh, q_tile;
+        fwd_item(w, p, kMode, &bh, &q_tile);
+        const int bb = bh / p.H, hh = bh % p.H;
+        Range rg[3];
+        const int nr = fwd_make_ranges<kMode>(p, q_tile * kFwdBM, rg);
+        const int qb = it & 1;
+        if (it >= 2) ok = mbar_wait(&q_empty[qb], ((it >> 1) - 1) & 1);
+        if (!ok) break;
+        mbar_expect_tx(&q_full[qb], kTile16);
+        tma_load_4d(&tm_q, &q_full[qb], smem + FwdSmem::kQ + qb * kTile16, 0, q_tile * kFwdBM, hh, bb);
+        for (int ri = 0; ri < nr && ok; ++ri) {
+          for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kFwdBN, ++J) {
+            const int st = J % kFwdStages;
+            if (J >= kFwdStages) ok = mbar_wait(&kv_empty[st], ((J / kFwdStages) - 1) & 1);
+            if (!ok) break;
+            mbar_expect_tx(&k_full[st], kTile16);
+            tma_load_4d(&tm_k, &k_full[st], smem + FwdSmem::kK + st * kTile16, 0, s, hh, bb);
+            mbar_expect_tx(&v_full[st], kTile16);
+            tma_load_4d(&tm_v, &v_full[st], smem + FwdSmem::kV + st * kTile16, 0, s, hh, bb);
+          }
         }
       }
     }
@@ -166,16 +191,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       constexpr uint32_t idesc_qk = idesc_f16(128, 128, false, false, kBF16);
       constexpr uint32_t idesc_pv = idesc_f16(128, 64, false, true, kBF16);
       const uint32_t sbase = smem_u32(smem);
-      const uint64_t qdesc = sw128_desc(sbase + FwdSmem::kQ, 16, 1024);
-      bool ok = mbar_wait(q_full, 0);
-      tc_fence_after();
-      // O_g += P_g V_jj[64g, 64g+64) for both halves, then release the K/V stage
-      auto issue_pv = [&](int jj) {
-        const int st = jj % kFwdStages;
-        ok = ok && mbar_wait(&v_full[st], (jj / kFwdStages) & 1);
-        const uint32_t sbuf = tmem + (jj & 1) * 128;
+      bool ok = true;
+      // O_g += P_g V_J[64g, 64g+64) for both halves, then release the K/V stage; the first PV
+      // of an item overwrites O, after the previous item's epilogue has read it
+      auto issue_pv = [&](int Jg, bool first, int it) {
+        const int st = Jg % kFwdStages;
+        ok = ok && mbar_wait(&v_full[st], (Jg / kFwdStages) & 1);
+        if (ok && first && it > 0) ok = mbar_wait(o_free, (it - 1) & 1);
+        const uint32_t sbuf = tmem + (Jg & 1) * 128;
         for (int g = 0; g < 2 && ok; ++g) {
-          ok = mbar_wait(&p_full[g], jj & 1);
+          ok = mbar_wait(&p_full[g], Jg & 1);
           if (!ok) break;
           tc_fence_after();
           const uint64_t vdesc = sw128_desc(
@@ -183,172 +208,216 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_ts(tmem + 256 + g * 64, sbuf + g * 64 + kk * 8, vdesc + ((kk * 2048) >> 4),
-                    idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+                    idesc_pv, (!first || kk > 0) ? 1u : 0u);
           umma_commit(&o_done[g]);
         }
         if (ok) umma_commit(&kv_empty[st]);
       };
-      int j = 0;
-      for (int ri = 0; ri < nr && ok; ++ri) {
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kFwdBN, ++j) {
-          const int st = j % kFwdStages;
-          ok = mbar_wait(&k_full[st], (j / kFwdStages) & 1);
+      int J = 0;  // key tiles issued so far by this CTA
+      for (int w = blockIdx.x, it = 0; w < num_items && ok; w += gridDim.x, ++it) {
+        int bh, q_tile;
+        fwd_item(w, p, kMode, &bh, &q_tile);
+        Range rg[3];
+        const int nr = fwd_make_ranges<kMode>(p, q_tile * kFwdBM, rg);
+        const int nt = fwd_count_tiles(rg, nr);
+        const int qb = it & 1;
+        ok = mbar_wait(&q_full[qb], (it >> 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t qdesc = sw128_desc(sbase + FwdSmem::kQ + qb * kTile16, 16, 1024);
+        for (int j = 0; j < nt && ok; ++j) {
+          const int Jg = J + j;
+          const int st = Jg % kFwdStages;
+          ok = mbar_wait(&k_full[st], (Jg / kFwdStages) & 1);
           if (!ok) break;
           tc_fence_after();
           const uint64_t kdesc = sw128_desc(sbase + FwdSmem::kK + st * kTile16, 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + (j & 1) * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
+            umma_ss(tmem + (Jg & 1) * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
                     idesc_qk, kk > 0 ? 1u : 0u);
-          umma_commit(&s_full[j & 1]);
-          if (j > 0) issue_pv(j - 1);
+          umma_commit(&s_full[Jg & 1]);
+          if (j == nt - 1) umma_commit(&q_empty[qb]);  // this item's Q is no longer read
+          if (j > 0) issue_pv(Jg - 1, j == 1, it);
         }
+        if (ok && nt > 0) issue_pv(J + nt - 1, nt == 1, it);
+        J += nt;
       }
-      if (ok && j > 0) issue_pv(j - 1);
     }
     __syncwarp();
   } else {
     // ---------------- softmax: warpgroup g owns key columns [64g, 64g+64) ----------------
     const int g = warp >> 2;
     const int row = threadIdx.x & 127;
-    const int qi = q_start + row;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const uint32_t tO = tmem + lane_base + 256 + g * 64;
-    float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
-    int j = 0;
-    for (int ri = 0; ri < nr && ok; ++ri) {
-      const int rule = rg[ri].rule, shift = rg[ri].shift;
-      // visible key interval of this row under the range's rule (absolute key indices)
-      int vlo = -2147483647, vhi = 2147483647;
-      if (kMode == kTrain) {
-        if (rule != 0) train_row_interval(rule, shift, qi, p.n, p.bs, &vlo, &vhi);
-      } else if (rule == 3) {
-        vlo = 0;
-        vhi = decode_row_hi(p.kv_len - p.q_len + qi, p.bs, p.kv_len);
-      }
-      for (int s = rg[ri].lo; s < rg[ri].hi; s += kFwdBN, ++j) {
-        const int b = j & 1;
-        ok = mbar_wait_warp(&s_full[b], (j >> 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t tS = tmem + lane_base + b * 128 + g * 64;
-        float x[64];
-        {
-          uint32_t r[2][32];
-          tmem_ld32_async(tS, r[0]);
-          tmem_ld32_async(tS + 32, r[1]);
-          tmem_ld_wait();
-#pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {
-            reg_fence(r[c2]);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) x[c2 * 32 + i] = __uint_as_float(r[c2][i]);
-          }
+    int J = 0;  // key tiles consumed so far by this CTA
+    for (int w = blockIdx.x, it = 0; w < num_items; w += gridDim.x, ++it) {
+      int bh, q_tile;
+      fwd_item(w, p, kMode, &bh, &q_tile);
+      const int bb = bh / p.H, hh = bh % p.H;
+      const int q_start = q_tile * kFwdBM;
+      const int qi = q_start + row;
+      Range rg[3];
+      const int nr = fwd_make_ranges<kMode>(p, q_start, rg);
+      float m_run = -INFINITY, l_run = 0.f;
+      int j = 0;
+      for (int ri = 0; ri < nr && ok; ++ri) {
+        const int rule = rg[ri].rule, shift = rg[ri].shift;
+        // visible key interval of this row under the range's rule (absolute key indices)
+        int vlo = -2147483647, vhi = 2147483647;
+        if (kMode == kTrain) {
+          if (rule != 0) train_row_interval(rule, shift, qi, p.n, p.bs, &vlo, &vhi);
+        } else if (rule == 3) {
+          vlo = 0;
+          vhi = decode_row_hi(p.kv_len - p.q_len + qi, p.bs, p.kv_len);
         }
-        if (rule != 0) {
-          const int lo = vlo - s - g * 64, hi = vhi - s - g * 64;
-#pragma unroll
-          for (int c = 0; c < 64; ++c)
-            if (c < lo || c >= hi) x[c] = -INFINITY;
-        }
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
-        mx *= p.scale_log2;
-        const float m_new = fmaxf(m_run, mx);
-        float alpha = 1.f;
-        bool rescale = false;
-        if (m_new - m_run > kRescaleLog2) {  // false for NaN (-inf - -inf)
-          alpha = ex2(m_run - m_new);        // 0 when m_run = -inf
-          rescale = (j > 0);
-          m_run = m_new;
-        }
-        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-        float sum = 0.f;
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2(fmaf(x[2 * i], p.scale_log2, -m_use));
-          const float p1 = ex2(fmaf(x[2 * i + 1], p.scale_log2, -m_use));
-          sum += p0 + p1;
-          pk[i] = pack2<kBF16>(p0, p1);
-        }
-        tmem_st32(tS, pk);  // P_g over this warpgroup's own (already read) S columns
-        l_run = l_run * alpha + sum;
-        tmem_st_wait();
-        if (j > 0) {
-          ok = mbar_wait_warp(&o_done[g], (j - 1) & 1);  // O_g += P_g V has landed
+        for (int s = rg[ri].lo; s < rg[ri].hi; s += kFwdBN, ++j) {
+          const int Jg = J + j;
+          const int b = Jg & 1;
+          ok = mbar_wait_warp(&s_full[b], (Jg >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
-        }
-        // the rescale's TMEM load/store is warp-collective: vote, and let the rows that do not
-        // need it multiply by alpha = 1
-        if (__any_sync(0xffffffffu, rescale)) {
-          uint32_t r[2][32];
-          tmem_ld32_async(tO, r[0]);
-          tmem_ld32_async(tO + 32, r[1]);
-          tmem_ld_wait();
+          const uint32_t tS = tmem + lane_base + b * 128 + g * 64;
+          float x[64];
+          {
+            uint32_t r[2][32];
+            tmem_ld32_async(tS, r[0]);
+            tmem_ld32_async(tS + 32, r[1]);
+            tmem_ld_wait();
 #pragma unroll
-          for (int c2 = 0; c2 < 2; ++c2) {
-            reg_fence(r[c2]);
+            for (int c2 = 0; c2 < 2; ++c2) {
+              reg_fence(r[c2]);
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              r[c2][i] = __float_as_uint(__uint_as_float(r[c2][i]) * alpha);
-            tmem_st32(tO + c2 * 32, r[c2]);
+              for (int i = 0; i < 32; ++i) x[c2 * 32 + i] = __uint_as_float(r[c2][i]);
+            }
           }
+          if (rule != 0) {
+            const int lo = vlo - s - g * 64, hi = vhi - s - g * 64;
+#pragma unroll
+            for (int c = 0; c < 64; ++c)
+              if (c < lo || c >= hi) x[c] = -INFINITY;
+          }
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 64; ++c) mx = fmaxf(mx, x[c]);
+          mx *= p.scale_log2;
+          const float m_new = fmaxf(m_run, mx);
+          float alpha = 1.f;
+          bool rescale = false;
+          if (m_new - m_run > kRescaleLog2) {  // false for NaN (-inf - -inf)
+            alpha = ex2(m_run - m_new);        // 0 when m_run = -inf
+            rescale = (j > 0);
+            m_run = m_new;
+          }
+          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+          float sum = 0.f;
+          uint32_t pk[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float p0 = ex2(fmaf(x[2 * i], p.scale_log2, -m_use));
+            const float p1 = ex2(fmaf(x[2 * i + 1], p.scale_log2, -m_use));
+            sum += p0 + p1;
+            pk[i] = pack2<kBF16>(p0, p1);
+          }
+          tmem_st32(tS, pk);  // P_g over this warpgroup's own (already read) S columns
+          l_run = l_run * alpha + sum;
           tmem_st_wait();
-        }
-        tc_fence_before();
-        mbar_arrive(&p_full[g]);
-      }
-    }
-    // ---- epilogue: both halves' last O_g += P_g V have landed; warpgroup 1 hands its
-    // (max, sum) to warpgroup 0, which merges O_0 and O_1 and stores O and the LSE ----
-    if (ok && j > 0) ok = mbar_wait_warp(&o_done[g], (j - 1) & 1);
-    ok = __all_sync(0xffffffffu, ok) && j > 0;
-    if (g == 1) {
-      merge_m[row] = m_run;
-      merge_l[row] = l_run;
-    }
-    tc_fence_before();
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    tc_fence_after();
-    if (g == 0 && ok) {
-      const float m1 = merge_m[row], l1 = merge_l[row];
-      const float M = fmaxf(m_run, m1);
-      const float Mu = (M == -INFINITY) ? 0.f : M;
-      const float w0 = ex2(m_run - Mu), w1 = ex2(m1 - Mu);  // 0 for a half that saw no key
-      const float L = l_run * w0 + l1 * w1;
-      const float a0 = w0 / L, a1 = w1 / L;
-      const int rows_valid = (kMode == kTrain) ? 2 * p.n : p.q_len;
-      const bool store = qi < rows_valid;
-      uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                      2 * (bb * p.o_sb + hh * p.o_sh + static_cast<long long>(qi) * p.o_ss);
+          if (j > 0) {
+            ok = mbar_wait_warp(&o_done[g], (Jg - 1) & 1);  // O_g += P_g V has landed
+            if (!ok) break;
+            tc_fence_after();
+          }
+          // the rescale's TMEM load/store is warp-collective: vote, and let the rows that do
+          // not need it multiply by alpha = 1
+          if (__any_sync(0xffffffffu, rescale)) {
+            uint32_t r[2][32];
+            tmem_ld32_async(tO, r[0]);
+            tmem_ld32_async(tO + 32, r[1]);
+            tmem_ld_wait();
 #pragma unroll
-      for (int c2 = 0; c2 < 2; ++c2) {
-        uint32_t r0[32], r1[32];
-        tmem_ld32_async(tmem + lane_base + 256 + c2 * 32, r0);
-        tmem_ld32_async(tmem + lane_base + 320 + c2 * 32, r1);
+            for (int c2 = 0; c2 < 2; ++c2) {
+              reg_fence(r[c2]);
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                r[c2][i] = __float_as_uint(__uint_as_float(r[c2][i]) * alpha);
+              tmem_st32(tO + c2 * 32, r[c2]);
+            }
+            tmem_st_wait();
+          }
+          tc_fence_before();
+          mbar_arrive(&p_full[g]);
+        }
+      }
+      // ---- epilogue: both halves' last O_g += P_g V have landed; warpgroup 1 hands its
+      // (max, sum) to warpgroup 0, which merges O_0 and O_1, stores O and the LSE, and frees
+      // the accumulators for the next item ----
+      if (ok && j > 0) ok = mbar_wait_warp(&o_done[g], (J + j - 1) & 1);
+      ok = __all_sync(0xffffffffu, ok);
+      float* merge_m = reinterpret_cast<float*>(smem + FwdSmem::kMerge) + (it & 1) * 256;
+      float* merge_l = merge_m + 128;
+      if (g == 1) {
+        merge_m[row] = m_run;
+        merge_l[row] = l_run;
+      }
+      tc_fence_before();
+      {  // both warpgroups meet here once per item and agree on whether to go on
+        uint32_t all;
+        asm volatile(
+            "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n"
+            " selp.u32 %0, 1, 0, q;\n}\n"
+            : "=r"(all)
+            : "r"(static_cast<uint32_t>(ok))
+            : "memory");
+        ok = all != 0;
+      }
+      tc_fence_after();
+      if (g == 0 && ok && j > 0) {
+        const float m1 = merge_m[row], l1 = merge_l[row];
+        const float M = fmaxf(m_run, m1);
+        const float Mu = (M == -INFINITY) ? 0.f : M;
+        const float w0 = ex2(m_run - Mu), w1 = ex2(m1 - Mu);  // 0 for a half that saw no key
+        const float L = l_run * w0 + l1 * w1;
+        const float a0 = w0 / L, a1 = w1 / L;
+        const int rows_valid = (kMode == kTrain) ? 2 * p.n : p.q_len;
+        const bool store = qi < rows_valid;
+        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
+                        2 * (bb * p.o_sb + hh * p.o_sh + static_cast<long long>(qi) * p.o_ss);
+        uint32_t r0[2][32], r1[2][32];
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          tmem_ld32_async(tmem + lane_base + 256 + c2 * 32, r0[c2]);
+          tmem_ld32_async(tmem + lane_base + 320 + c2 * 32, r1[c2]);
+        }
         tmem_ld_wait();
-        reg_fence(r0);
-        reg_fence(r1);
-        uint32_t packed[16];
+        tc_fence_before();
+        mbar_arrive(o_free);  // O_0 and O_1 are in registers: the next item may overwrite them
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          packed[i] = pack2<kBF16>(
-              __uint_as_float(r0[2 * i]) * a0 + __uint_as_float(r1[2 * i]) * a1,
-              __uint_as_float(r0[2 * i + 1]) * a0 + __uint_as_float(r1[2 * i + 1]) * a1);
-        uint4* dst = reinterpret_cast<uint4*>(orow + c2 * 64);
-        if (store) {
+        for (int c2 = 0; c2 < 2; ++c2) {
+          reg_fence(r0[c2]);
+          reg_fence(r1[c2]);
+          uint32_t packed[16];
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                                packed[4 * i + 3]);
+          for (int i = 0; i < 16; ++i)
+            packed[i] = pack2<kBF16>(
+                __uint_as_float(r0[c2][2 * i]) * a0 + __uint_as_float(r1[c2][2 * i]) * a1,
+                __uint_as_float(r0[c2][2 * i + 1]) * a0 + __uint_as_float(r1[c2][2 * i + 1]) * a1);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c2 * 64);
+          if (store) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
+                                  packed[4 * i + 3]);
+          }
         }
+        if (store && p.lse != nullptr)
+          p.lse[bb * p.lse_sb + hh * p.lse_sh + qi] = (Mu + __log2f(L)) * 0.69314718055994530942f;
+      } else if (g == 0) {
+        mbar_arrive(o_free);  // keep the phase count in step with the issuer
       }
-      if (store && p.lse != nullptr)
-        p.lse[bb * p.lse_sb + hh * p.lse_sh + qi] = (Mu + __log2f(L)) * 0.69314718055994530942f;
+      J += j;
+      if (!ok) break;
     }
   }
   tc_fence_before();

@@ -209,9 +209,13 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   p.kv_len = static_cast<int>(kv_len);
   p.bs = static_cast<int>(bs);
   p.num_q_tiles = static_cast<int>(bd3::cdiv(static_cast<int>(q_rows), bd3::kFwdBM));
+  p.num_bh = static_cast<int>(B * H);
   p.scale_log2 = 0.125f * 1.4426950408889634f;
-  const int64_t grid = B * H * p.num_q_tiles;
-  if (grid > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "grid too large");
+  const int64_t items = B * H * p.num_q_tiles;
+  if (items > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "too many query tiles");
+  int sms = 148;
+  if ((rc = current_device_sms(&sms)) != BD3_OK) return rc;
+  const int64_t grid = items < sms ? items : sms;  // persistent: one CTA per SM
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const bd3::FwdParams);
   int slot;
   if (mode == bd3::kTrain) {
