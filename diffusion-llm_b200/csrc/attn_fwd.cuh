@@ -13,7 +13,8 @@
 // and O accumulator (an in-CTA split of the keys), and the two halves are merged once at the
 // end with the split-KV weighting. No per-tile exchange between the warpgroups is needed.
 // Roles (320 threads):
-//   warps 0-3  softmax, key columns [0,64) of every tile: thread t owns query row t (TMEM lane t)
+//   warps 0-3  softmax, key columns [0,64) of every tile: thread t owns query row t (TMEM lane
+//              t); at each item's end they merge the halves and write O with a TMA store
 //   warps 4-7  softmax, key columns [64,128)
 //   warp 8     TMA producer: each item's Q tile, then its K and V tiles into the ring
 //   warp 9     TMEM owner and UMMA issuer (one thread):
@@ -59,7 +60,8 @@ struct FwdSmem {
   static constexpr uint32_t kQ = 0;                          // [item parity]
   static constexpr uint32_t kK = kQ + 2 * kTile16;
   static constexpr uint32_t kV = kK + kFwdStages * kTile16;
-  static constexpr uint32_t kBar = kV + kFwdStages * kTile16;
+  static constexpr uint32_t kOut = kV + kFwdStages * kTile16;  // O staging for the TMA store
+  static constexpr uint32_t kBar = kOut + kTile16;
   // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[2], p_full[2],
   // o_done[2], o_free
   static constexpr uint32_t kNumBars = 4 + 3 * kFwdStages + 7;
@@ -86,6 +88,25 @@ __device__ __forceinline__ int fwd_make_ranges(const FwdParams& p, int q_start, 
   return decode_ranges(q_start, kFwdBM, kFwdBN, p.q_len, p.kv_len, p.bs, r);
 }
 
+// TMA store of a 128-row x 64-element 16-bit box from shared memory (128-byte swizzle).
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0,
+                                             int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::
+          "l"(reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group_fwd() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group_read0_fwd() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_group0_fwd() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // Decode work item w of the persistent loop: its (batch*head) and query tile.
 __device__ __forceinline__ void fwd_item(int w, const FwdParams& p, int mode, int* bh,
                                          int* q_tile) {
@@ -104,7 +125,8 @@ template <int kMode, bool kBF16>
 __global__ void __launch_bounds__(kFwdThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
-                    const __grid_constant__ CUtensorMap tm_v, const FwdParams p) {
+                    const __grid_constant__ CUtensorMap tm_v,
+                    const __grid_constant__ CUtensorMap tm_o, const FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -213,36 +235,49 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         }
         if (ok) umma_commit(&kv_empty[st]);
       };
-      int J = 0;  // key tiles issued so far by this CTA
-      for (int w = blockIdx.x, it = 0; w < num_items && ok; w += gridDim.x, ++it) {
-        int bh, q_tile;
-        fwd_item(w, p, kMode, &bh, &q_tile);
-        Range rg[3];
-        const int nr = fwd_make_ranges<kMode>(p, q_tile * kFwdBM, rg);
-        const int nt = fwd_count_tiles(rg, nr);
-        const int qb = it & 1;
-        ok = mbar_wait(&q_full[qb], (it >> 1) & 1);
-        if (!ok) break;
-        tc_fence_after();
-        const uint64_t qdesc = sw128_desc(sbase + FwdSmem::kQ + qb * kTile16, 16, 1024);
-        for (int j = 0; j < nt && ok; ++j) {
-          const int Jg = J + j;
-          const int st = Jg % kFwdStages;
-          ok = mbar_wait(&k_full[st], (Jg / kFwdStages) & 1);
+      // One flat loop over this CTA's key tiles across its items: S(J) is issued before
+      // O += P V of tile J-1, also across item boundaries, so the S buffers never drain.
+      int J = 0;                 // key tiles issued so far by this CTA
+      int it = -1, w = blockIdx.x - static_cast<int>(gridDim.x), nt = 0, j = 0;
+      uint64_t qdesc = 0;
+      int prev_J = -1, prev_it = 0;
+      bool prev_first = false;
+      while (ok) {
+        if (j == nt) {  // next item (an item always has at least one key tile)
+          w += gridDim.x;
+          ++it;
+          if (w >= num_items) break;
+          int bh, q_tile;
+          fwd_item(w, p, kMode, &bh, &q_tile);
+          Range rg[3];
+          const int nr = fwd_make_ranges<kMode>(p, q_tile * kFwdBM, rg);
+          nt = fwd_count_tiles(rg, nr);
+          j = 0;
+          const int qb = it & 1;
+          ok = mbar_wait(&q_full[qb], (it >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t kdesc = sw128_desc(sbase + FwdSmem::kK + st * kTile16, 16, 1024);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_ss(tmem + (Jg & 1) * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
-                    idesc_qk, kk > 0 ? 1u : 0u);
-          umma_commit(&s_full[Jg & 1]);
-          if (j == nt - 1) umma_commit(&q_empty[qb]);  // this item's Q is no longer read
-          if (j > 0) issue_pv(Jg - 1, j == 1, it);
+          qdesc = sw128_desc(sbase + FwdSmem::kQ + qb * kTile16, 16, 1024);
         }
-        if (ok && nt > 0) issue_pv(J + nt - 1, nt == 1, it);
-        J += nt;
+        const int st = J % kFwdStages;
+        ok = mbar_wait(&k_full[st], (J / kFwdStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t kdesc = sw128_desc(sbase + FwdSmem::kK + st * kTile16, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_ss(tmem + (J & 1) * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
+                  idesc_qk, kk > 0 ? 1u : 0u);
+        umma_commit(&s_full[J & 1]);
+        if (j == nt - 1) umma_commit(&q_empty[it & 1]);  // this item's Q is no longer read
+        if (prev_J >= 0) issue_pv(prev_J, prev_first, prev_it);
+        prev_J = J;
+        prev_first = (j == 0);
+        prev_it = it;
+        ++J;
+        ++j;
       }
+      if (ok && prev_J >= 0) issue_pv(prev_J, prev_first, prev_it);
     }
     __syncwarp();
   } else {
@@ -381,9 +416,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         const float L = l_run * w0 + l1 * w1;
         const float a0 = w0 / L, a1 = w1 / L;
         const int rows_valid = (kMode == kTrain) ? 2 * p.n : p.q_len;
-        const bool store = qi < rows_valid;
-        uint8_t* orow = reinterpret_cast<uint8_t*>(p.o) +
-                        2 * (bb * p.o_sb + hh * p.o_sh + static_cast<long long>(qi) * p.o_ss);
         uint32_t r0[2][32], r1[2][32];
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
@@ -393,6 +425,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(o_free);  // O_0 and O_1 are in registers: the next item may overwrite them
+        // O goes out through a swizzled shared-memory tile and one TMA store (rows past the
+        // end of a ragged prefill tile are clipped by the tensor map)
+        const bool leader = (threadIdx.x == 0);
+        uint8_t* stage = smem + FwdSmem::kOut;
+        if (leader) bulk_wait_group_read0_fwd();  // the previous item's store has read it
+        asm volatile("bar.sync 2, 128;" ::: "memory");
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2) {
           reg_fence(r0[c2]);
@@ -403,15 +441,18 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
             packed[i] = pack2<kBF16>(
                 __uint_as_float(r0[c2][2 * i]) * a0 + __uint_as_float(r1[c2][2 * i]) * a1,
                 __uint_as_float(r0[c2][2 * i + 1]) * a0 + __uint_as_float(r1[c2][2 * i + 1]) * a1);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c2 * 64);
-          if (store) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2],
-                                  packed[4 * i + 3]);
-          }
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(stage + sw128_offset(row, c2 * 4 + i)) =
+                make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
         }
-        if (store && p.lse != nullptr)
+        fence_proxy_async_smem();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (leader) {
+          tma_store_4d(&tm_o, stage, 0, q_start, hh, bb);
+          bulk_commit_group_fwd();
+        }
+        if (qi < rows_valid && p.lse != nullptr)
           p.lse[bb * p.lse_sb + hh * p.lse_sh + qi] = (Mu + __log2f(L)) * 0.69314718055994530942f;
       } else if (g == 0) {
         mbar_arrive(o_free);  // keep the phase count in step with the issuer
@@ -420,6 +461,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       if (!ok) break;
     }
   }
+  if (threadIdx.x == 0) bulk_wait_group0_fwd();  // the last O store has landed
   tc_fence_before();
   __syncthreads();
   if (warp == 9) {

@@ -195,6 +195,8 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   const int64_t* so = strides + 9;
   if (reinterpret_cast<uintptr_t>(o) % 16 || so[0] % 8 || so[1] % 8 || so[2] % 8)
     return fail(BD3_ERR_INVALID, "o: pointer and strides must be 16-byte aligned");
+  CUtensorMap to;
+  if ((rc = make_map(&to, o, dtype, q_rows, H, B, so, bd3::kFwdBM, "o")) != BD3_OK) return rc;
   bd3::FwdParams p{};
   p.o = o;
   p.lse = lse;
@@ -216,7 +218,8 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   int sms = 148;
   if ((rc = current_device_sms(&sms)) != BD3_OK) return rc;
   const int64_t grid = items < sms ? items : sms;  // persistent: one CTA per SM
-  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const bd3::FwdParams);
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
+               const bd3::FwdParams);
   int slot;
   if (mode == bd3::kTrain) {
     kern = dtype == BD3_BF16 ? bd3::attn_fwd_kernel<bd3::kTrain, true>
@@ -229,7 +232,7 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   }
   if ((rc = set_smem(kern, bd3::FwdSmem::kAlloc, slot)) != BD3_OK) return rc;
   ProfScope ps(mode == bd3::kTrain ? kPfFwd : kPfPrefill, stream);
-  kern<<<static_cast<unsigned>(grid), bd3::kFwdThreads, bd3::FwdSmem::kAlloc, stream>>>(tq, tk, tv, p);
+  kern<<<static_cast<unsigned>(grid), bd3::kFwdThreads, bd3::FwdSmem::kAlloc, stream>>>(tq, tk, tv, to, p);
   return check_launch("attn_fwd_kernel launch");
 }
 
