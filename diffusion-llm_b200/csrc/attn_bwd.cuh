@@ -6,8 +6,9 @@
 //
 //   bwd_prep_kernel     Delta = rowsum(dO * O) and LSE * log2(e) per query row (fp32), and
 //                       zeroes the fp32 dQ accumulator.
-//   bwd_fused_kernel    one CTA per (batch*head, 128-key tile), stepping over the query ranges
-//                       that see the tile (the reference's dK/dV ranges, :274-325):
+//   bwd_fused_kernel    persistent: one CTA per SM loops over (batch*head, 128-key tile) items,
+//                       heaviest first, stepping over the query ranges that see each tile (the
+//                       reference's dK/dV ranges, :274-325):
 //                         S^T  = K Q_i^T,  dP^T = V dO_i^T          (SS MMAs, keys on TMEM lanes)
 //                         P^T  = exp2(S^T * scale*log2e - L2[q]) masked to 0,
 //                         dS^T = P^T * (dP^T - Delta[q])            (element-wise, thread = key)
@@ -19,14 +20,19 @@
 //   bwd_dq_convert_kernel  dQ = scale * accumulator, in the input dtype.
 //
 // Each 128-query step runs as two 64-query halves whose S^T/dP^T live in two TMEM buffers, so
-// the MMAs of one half overlap the element-wise pass over the other.
-// Roles in the fused kernel (448 threads):
-//   warps 0-7  element-wise: two warpgroups; thread t of each owns key row t (TMEM lane t),
-//              warpgroup g takes queries [32g, 32g+32) of every half-step
-//   warps 8-11 dQ reducer: thread t owns query row t of dQ_i (TMEM lane t); stages dQ_i in
-//              shared memory and adds it to the fp32 accumulator with TMA reduce-adds
-//   warp 12    TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
-//   warp 13    TMEM owner and UMMA issuer
+// the MMAs of one half overlap the element-wise pass over the other. K/V are double-buffered
+// across items (the next item's tiles load during the current one), the step and half-step
+// counters behind every barrier phase run on across items, and an item's dV/dK epilogue
+// overlaps the next item's first S^T/dP^T.
+// Roles in the fused kernel (704 threads):
+//   warps 0-15  element-wise: four warpgroups; thread t of each owns key row t (TMEM lane t),
+//               warpgroup g takes queries [16g, 16g+16) of every half-step (four warps per
+//               SM sub-partition keep the exponential and FMA pipes busy)
+//   warps 16-19 dQ reducer and dV/dK writer: thread t owns row t (TMEM lane t); stages dQ_i
+//               in shared memory and adds it to the fp32 accumulator with TMA reduce-adds, and
+//               writes each item's dV and dK tiles with TMA stores
+//   warp 20     TMA producer: K, V once; Q_i, dO_i (and their LSE/Delta rows) per step
+//   warp 21     TMEM owner and UMMA issuer
 // TMEM columns: half-step buffers [0,128) and [128,256) (S^T then dP^T, 64 columns each),
 // dV [256,320), dK [320,384), dQ_i [384,448). P^T and dS^T (packed 16-bit) overwrite the
 // columns each thread has already read. dS for the dQ MMA lives in shared memory (two
@@ -43,7 +49,7 @@ namespace bd3 {
 constexpr int kBwdBKV = 128;  // keys per CTA
 constexpr int kBwdBQ = 128;   // queries per step
 constexpr int kBwdStages = 2;
-constexpr int kBwdThreads = 448;
+constexpr int kBwdThreads = 704;
 
 struct BwdParams {
   const void* o;
@@ -59,6 +65,7 @@ struct BwdParams {
   long long dq_sb, dq_sh, dq_ss, dk_sb, dk_sh, dk_ss, dv_sb, dv_sh, dv_ss;
   int H, n, bs;
   int num_tiles;         // key tiles per (batch, head)
+  int num_bh;            // batch * heads
   float scale, scale_log2;
 };
 
@@ -152,41 +159,23 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const BwdParams p, 
                  pack2<kBF16>(y.x * s, y.y * s), pack2<kBF16>(y.z * s, y.w * s));
 }
 
-// Store 64 fp32 accumulator columns of one row (read from TMEM) as 16-bit values * mul.
-template <bool kBF16>
-__device__ __forceinline__ void store_row64(uint32_t taddr, void* dst, float mul) {
-  uint4* d4 = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int c2 = 0; c2 < 2; ++c2) {
-    uint32_t r[32];
-    tmem_ld32(taddr + c2 * 32, r);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      d4[c2 * 4 + i] = make_uint4(
-          pack2<kBF16>(__uint_as_float(r[8 * i + 0]) * mul, __uint_as_float(r[8 * i + 1]) * mul),
-          pack2<kBF16>(__uint_as_float(r[8 * i + 2]) * mul, __uint_as_float(r[8 * i + 3]) * mul),
-          pack2<kBF16>(__uint_as_float(r[8 * i + 4]) * mul, __uint_as_float(r[8 * i + 5]) * mul),
-          pack2<kBF16>(__uint_as_float(r[8 * i + 6]) * mul, __uint_as_float(r[8 * i + 7]) * mul));
-  }
-}
-
 struct BwdSmem {
-  static constexpr uint32_t kK = 0;
-  static constexpr uint32_t kV = kK + kTile16;
-  static constexpr uint32_t kQ = kV + kTile16;                  // [stage]
+  static constexpr uint32_t kK = 0;                             // [item parity]
+  static constexpr uint32_t kV = kK + 2 * kTile16;              // [item parity]
+  static constexpr uint32_t kQ = kV + 2 * kTile16;              // [stage]
   static constexpr uint32_t kDO = kQ + kBwdStages * kTile16;    // [stage]
   static constexpr uint32_t kDS = kDO + kBwdStages * kTile16;   // [buffer][q half][key][128 B]
   static constexpr uint32_t kVec = kDS + 2 * 2 * kTile16;       // [stage][L2 128 | Delta 128]
-  static constexpr uint32_t kRed = kVec + kBwdStages * 1024;    // dQ_i staging: [2 boxes][128][128 B]
-  static constexpr uint32_t kBar = kRed + 2 * kTile16;
-  // kv_full, qd_full[S], qd_empty[S], s_full[2], p_full[2], ds_free[2], dq_full, dq_empty,
-  // acc_done
-  static constexpr uint32_t kNumBars = 1 + 2 * kBwdStages + 6 + 3;
+  static constexpr uint32_t kRed = kVec + kBwdStages * 1024;    // dQ_i staging: one [128][128 B] box
+  static constexpr uint32_t kBar = kRed + kTile16;
+  // kv_full[2], kv_empty[2], qd_full[S], qd_empty[S], s_full[2], p_full[2], ds_free[2],
+  // dq_full, dq_empty, acc_done, acc_free
+  static constexpr uint32_t kNumBars = 4 + 2 * kBwdStages + 6 + 4;
   static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
   static constexpr uint32_t kAlloc = kTmemSlot + 16 + 1024;
 };
 
-// Key tile processed by linear CTA index t: the clean key tiles near the start of the clean
+// Key tile of the t-th group of work items: the clean key tiles near the start of the clean
 // copy are seen by the most query tiles, so they go first; noisy tiles (one step) last.
 __device__ __forceinline__ int bwd_tile_order(int t, int num_tiles) {
   const int half = num_tiles / 2;
@@ -195,56 +184,77 @@ __device__ __forceinline__ int bwd_tile_order(int t, int num_tiles) {
 }
 
 // Column of the packed 16-bit P^T / dS^T operand for k-step kk (16 queries) of a half-step:
-// element-wise warpgroup g writes queries [32g, 32g+32) of the half into its own 32 read
-// columns, so queries [0,32) sit at columns [0,16) and [32,64) at [32,48).
-__device__ __forceinline__ uint32_t half_ts_col(int kk) { return kk < 2 ? kk * 8 : 32 + (kk - 2) * 8; }
+// element-wise warpgroup g writes queries [16g, 16g+16) of the half, packed, into the first 8
+// of its own 16 read columns, so k-step kk sits at columns [16kk, 16kk+8).
+__device__ __forceinline__ uint32_t half_ts_col(int kk) { return static_cast<uint32_t>(kk) * 16; }
+
+// Work item w of the persistent loop: one key tile of one (batch, head). Items are numbered
+// heaviest first (bwd_tile_order), so a round-robin over CTAs balances the steps.
+struct BwdItem {
+  int bb, hh, k_start, nr, nsteps;
+  long long row0;  // first row of this (batch, head) in the flattened (B*H*2n) row space
+  Range rg[4];
+};
+__device__ __forceinline__ void bwd_item(int w, const BwdParams& p, BwdItem* t) {
+  const int bh = w % p.num_bh;
+  t->k_start = bwd_tile_order(w / p.num_bh, p.num_tiles) * kBwdBKV;
+  t->bb = bh / p.H;
+  t->hh = bh % p.H;
+  t->row0 = static_cast<long long>(bh) * 2 * p.n;
+  t->nr = dkdv_ranges(t->k_start, kBwdBKV, kBwdBQ, p.n, p.bs, t->rg);
+  int ns = 0;
+  for (int r = 0; r < t->nr; ++r)
+    if (t->rg[r].hi > t->rg[r].lo) ns += cdiv(t->rg[r].hi - t->rg[r].lo, kBwdBQ);
+  t->nsteps = ns;
+}
 
 template <bool kBF16>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                     const __grid_constant__ CUtensorMap tm_dqacc, const BwdParams p) {
+                     const __grid_constant__ CUtensorMap tm_dqacc,
+                     const __grid_constant__ CUtensorMap tm_dk, const __grid_constant__ CUtensorMap tm_dv,
+                     const BwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BwdSmem::kBar);
-  uint64_t* kv_full = bars;
-  uint64_t* qd_full = bars + 1;
-  uint64_t* qd_empty = bars + 1 + kBwdStages;
-  uint64_t* s_full = bars + 1 + 2 * kBwdStages;  // [half]
+  uint64_t* kv_full = bars;                       // [item parity]
+  uint64_t* kv_empty = bars + 2;                  // [item parity]
+  uint64_t* qd_full = bars + 4;                   // [stage]
+  uint64_t* qd_empty = bars + 4 + kBwdStages;     // [stage]
+  uint64_t* s_full = bars + 4 + 2 * kBwdStages;   // [half]
   uint64_t* p_full = s_full + 2;                  // [half]
   uint64_t* ds_free = s_full + 4;                 // [dS buffer]
   uint64_t* dq_full = s_full + 6;
   uint64_t* dq_empty = s_full + 7;
-  uint64_t* acc_done = s_full + 8;
+  uint64_t* acc_done = s_full + 8;                // an item's dV/dK accumulators are final
+  uint64_t* acc_free = s_full + 9;                // ... and have been read out
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + BwdSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
-  const int BH = gridDim.x / p.num_tiles;
-  const int bh = blockIdx.x % BH;
-  const int k_tile = bwd_tile_order(blockIdx.x / BH, p.num_tiles);
-  const int k_start = k_tile * kBwdBKV;
-  const int bb = bh / p.H, hh = bh % p.H;
-  const long long row0 = static_cast<long long>(bh) * 2 * p.n;  // first row of this (b, h)
-  Range rg[4];
-  const int nr = dkdv_ranges(k_start, kBwdBKV, kBwdBQ, p.n, p.bs, rg);
+  const int num_items = p.num_bh * p.num_tiles;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&kv_full[b], 1);
+      mbar_init(&kv_empty[b], 1);
+    }
     for (int s = 0; s < kBwdStages; ++s) {
       mbar_init(&qd_full[s], 1);
       mbar_init(&qd_empty[s], 1);
     }
     for (int h = 0; h < 2; ++h) {
       mbar_init(&s_full[h], 1);
-      mbar_init(&p_full[h], 256);
+      mbar_init(&p_full[h], 512);
       mbar_init(&ds_free[h], 1);
     }
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 128);
     mbar_init(acc_done, 1);
+    mbar_init(acc_free, 128);
     fence_mbar_init();
   }
-  if (warp == 13) {
+  if (warp == 21) {
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
@@ -256,249 +266,333 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // dV [256,320), dK [320,384), dQ [384,448)
   constexpr uint32_t tDV = 256, tDK = 320, tDQ = 384;
 
-  if (warp == 12) {
-    // ---------------- TMA producer ----------------
+  if (warp == 20) {
+    // ---------------- TMA producer: per item K, V; per step Q_i, dO_i, L2_i, Delta_i --------
     if (elect_one()) {
       bool ok = true;
-      mbar_expect_tx(kv_full, 2 * kTile16);
-      tma_load_4d(&tm_k, kv_full, smem + BwdSmem::kK, 0, k_start, hh, bb);
-      tma_load_4d(&tm_v, kv_full, smem + BwdSmem::kV, 0, k_start, hh, bb);
-      int i = 0;
-      for (int ri = 0; ri < nr && ok; ++ri)
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdBQ, ++i) {
-          const int st = i % kBwdStages;
-          if (i >= kBwdStages) ok = mbar_wait(&qd_empty[st], ((i / kBwdStages) - 1) & 1);
-          if (!ok) break;
-          mbar_expect_tx(&qd_full[st], 2 * kTile16 + 1024);
-          tma_load_4d(&tm_q, &qd_full[st], smem + BwdSmem::kQ + st * kTile16, 0, s, hh, bb);
-          tma_load_4d(&tm_do, &qd_full[st], smem + BwdSmem::kDO + st * kTile16, 0, s, hh, bb);
-          uint8_t* vec = smem + BwdSmem::kVec + st * 1024;
-          bulk_load(vec, p.lse2 + row0 + s, 512, &qd_full[st]);
-          bulk_load(vec + 512, p.delta + row0 + s, 512, &qd_full[st]);
-        }
+      int it = 0, i = 0;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        BwdItem t;
+        bwd_item(w, p, &t);
+        if (t.nsteps == 0) continue;
+        const int kb = it & 1;
+        if (it >= 2) ok = mbar_wait(&kv_empty[kb], ((it >> 1) - 1) & 1);
+        if (!ok) break;
+        mbar_expect_tx(&kv_full[kb], 2 * kTile16);
+        tma_load_4d(&tm_k, &kv_full[kb], smem + BwdSmem::kK + kb * kTile16, 0, t.k_start, t.hh, t.bb);
+        tma_load_4d(&tm_v, &kv_full[kb], smem + BwdSmem::kV + kb * kTile16, 0, t.k_start, t.hh, t.bb);
+        for (int ri = 0; ri < t.nr && ok; ++ri)
+          for (int s = t.rg[ri].lo; s < t.rg[ri].hi && ok; s += kBwdBQ, ++i) {
+            const int st = i % kBwdStages;
+            if (i >= kBwdStages) ok = mbar_wait(&qd_empty[st], ((i / kBwdStages) - 1) & 1);
+            if (!ok) break;
+            mbar_expect_tx(&qd_full[st], 2 * kTile16 + 1024);
+            tma_load_4d(&tm_q, &qd_full[st], smem + BwdSmem::kQ + st * kTile16, 0, s, t.hh, t.bb);
+            tma_load_4d(&tm_do, &qd_full[st], smem + BwdSmem::kDO + st * kTile16, 0, s, t.hh, t.bb);
+            uint8_t* vec = smem + BwdSmem::kVec + st * 1024;
+            bulk_load(vec, p.lse2 + t.row0 + s, 512, &qd_full[st]);
+            bulk_load(vec + 512, p.delta + t.row0 + s, 512, &qd_full[st]);
+          }
+        ++it;
+      }
     }
     __syncwarp();
-  } else if (warp == 13) {
+  } else if (warp == 21) {
     // ---------------- UMMA issuer ----------------
     if (elect_one()) {
       constexpr uint32_t idesc_s = idesc_f16(128, 64, false, false, kBF16);
       constexpr uint32_t idesc_ts = idesc_f16(128, 64, false, true, kBF16);
       constexpr uint32_t idesc_dq = idesc_f16(128, 64, true, true, kBF16);
       const uint32_t sbase = smem_u32(smem);
-      const uint64_t kdesc = sw128_desc(sbase + BwdSmem::kK, 16, 1024);
-      const uint64_t vdesc = sw128_desc(sbase + BwdSmem::kV, 16, 1024);
-      const uint64_t kmn = sw128_desc(sbase + BwdSmem::kK, kTile16, 1024);
-      bool ok = mbar_wait(kv_full, 0);
-      // dV/dK of half-step jp (and, when it completes a step, that step's dQ)
-      auto finish = [&](int jp) {
-        const int hp = jp & 1, ip = jp >> 1, stp = ip % kBwdStages;
+      bool ok = true;
+      // A half-step whose dV/dK MMAs are still to be issued: global half index j, its Q/dO
+      // stage, its item (counted over this CTA's items), and whether it is the item's first or
+      // last half.
+      struct Half {
+        int j, st, it;
+        bool first, last;
+      };
+      Half prev{-1, 0, 0, false, false};
+      int pend_i = -1, pend_kb = 0;  // step whose dQ MMA is still to be issued, its K buffer
+      bool pend_last = false;        // ... and whether it is its item's last step
+      // dV += P^T dO_i, dK += dS^T Q_i of one half-step; a step's last half frees its Q/dO
+      // stage and queues its dQ; an item's last half publishes dV/dK.
+      auto finish = [&](const Half& hf) {
+        const int hp = hf.j & 1, ip = hf.j >> 1;
         ok = ok && mbar_wait(&p_full[hp], ip & 1);
         if (!ok) return;
+        if (hf.first && hf.it > 0) {  // the previous item's dV/dK have been read out
+          ok = mbar_wait(acc_free, (hf.it - 1) & 1);
+          if (!ok) return;
+        }
         tc_fence_after();
-        const uint32_t qa = sbase + BwdSmem::kQ + stp * kTile16 + hp * (kTile16 / 2);
-        const uint32_t da = sbase + BwdSmem::kDO + stp * kTile16 + hp * (kTile16 / 2);
+        const uint32_t qa = sbase + BwdSmem::kQ + hf.st * kTile16 + hp * (kTile16 / 2);
+        const uint32_t da = sbase + BwdSmem::kDO + hf.st * kTile16 + hp * (kTile16 / 2);
         const uint64_t domn = sw128_desc(da, kTile16, 1024);
         const uint64_t qmn = sw128_desc(qa, kTile16, 1024);
         const uint32_t tbuf = tmem + hp * 128;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_ts(tmem + tDV, tbuf + half_ts_col(kk), domn + ((kk * 2048) >> 4), idesc_ts,
-                  (jp > 0 || kk > 0) ? 1u : 0u);
+                  (hf.first && kk == 0) ? 0u : 1u);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_ts(tmem + tDK, tbuf + 64 + half_ts_col(kk), qmn + ((kk * 2048) >> 4), idesc_ts,
-                  (jp > 0 || kk > 0) ? 1u : 0u);
-        if (hp == 1) {  // step ip is complete: its Q/dO stage is free, and dQ can run
-          umma_commit(&qd_empty[stp]);
-          if (ip > 0) {
-            ok = mbar_wait(dq_empty, (ip - 1) & 1);  // the reducer has read dQ_{ip-1}
-            if (!ok) return;
-            tc_fence_after();
-          }
-          const uint64_t dsdesc =
-              sw128_desc(sbase + BwdSmem::kDS + (ip & 1) * 2 * kTile16, kTile16, 1024);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            umma_ss(tmem + tDQ, dsdesc + ((kk * 2048) >> 4), kmn + ((kk * 2048) >> 4),
-                    idesc_dq, kk > 0 ? 1u : 0u);
-          umma_commit(dq_full);
-          umma_commit(&ds_free[ip & 1]);
+                  (hf.first && kk == 0) ? 0u : 1u);
+        if (hp == 1) {
+          umma_commit(&qd_empty[hf.st]);
+          pend_i = ip;
+          pend_kb = hf.it & 1;
+          pend_last = hf.last;
         }
+        if (hf.last) umma_commit(acc_done);
       };
-      int j = 0;
-      int i = 0;
-      for (int ri = 0; ri < nr && ok; ++ri)
-        for (int s = rg[ri].lo; s < rg[ri].hi && ok; s += kBwdBQ, ++i) {
-          const int st = i % kBwdStages;
-          ok = mbar_wait(&qd_full[st], (i / kBwdStages) & 1);
-          if (!ok) break;
+      // dQ_i = dS_i K. Issued after the next half-step's S^T/dP^T, which the element-wise
+      // warps wait for, while dQ only feeds the reducer. An item's last dQ is the last reader
+      // of its K/V buffer.
+      auto issue_dq = [&]() {
+        if (pend_i > 0) {
+          ok = mbar_wait(dq_empty, (pend_i - 1) & 1);  // the reducer has read dQ_{i-1}
+          if (!ok) return;
           tc_fence_after();
-#pragma unroll
-          for (int h = 0; h < 2; ++h, ++j) {
-            const uint32_t qa = sbase + BwdSmem::kQ + st * kTile16 + h * (kTile16 / 2);
-            const uint32_t da = sbase + BwdSmem::kDO + st * kTile16 + h * (kTile16 / 2);
-            const uint64_t qdesc = sw128_desc(qa, 16, 1024);
-            const uint64_t dodesc = sw128_desc(da, 16, 1024);
-            const uint32_t tbuf = tmem + h * 128;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_ss(tbuf, kdesc + kk * 2, qdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              umma_ss(tbuf + 64, vdesc + kk * 2, dodesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[h]);
-            if (j > 0) finish(j - 1);
-            if (!ok) break;
-          }
         }
-      if (ok && j > 0) finish(j - 1);
-      umma_commit(acc_done);
-    }
-    __syncwarp();
-  } else if (warp >= 8) {
-    // ---------------- dQ reducer: thread = query row of the step ----------------
-    // dQ_i goes from TMEM to a swizzled shared-memory tile (two 32-column boxes) and from
-    // there into the fp32 accumulator by two TMA reduce-adds, so the additions run in L2
-    // without occupying this SM's load/store path.
-    const int row = threadIdx.x - 256;
-    const bool leader = (threadIdx.x == 256);
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint8_t* stage = smem + BwdSmem::kRed;
-    bool ok = true;
-    int i = 0;
-    for (int ri = 0; ri < nr && ok; ++ri)
-      for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
-        ok = mbar_wait_warp(dq_full, i & 1);
-        // the four reducer warps share named barriers below: agree on leaving the loop
-        {
-          uint32_t all;
-          asm volatile(
-              "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 2, 128, p;\n"
-              " selp.u32 %0, 1, 0, q;\n}\n"
-              : "=r"(all)
-              : "r"(static_cast<uint32_t>(ok))
-              : "memory");
-          ok = all != 0;
-        }
+        const uint64_t kmn = sw128_desc(sbase + BwdSmem::kK + pend_kb * kTile16, kTile16, 1024);
+        const uint64_t dsdesc =
+            sw128_desc(sbase + BwdSmem::kDS + (pend_i & 1) * 2 * kTile16, kTile16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          umma_ss(tmem + tDQ, dsdesc + ((kk * 2048) >> 4), kmn + ((kk * 2048) >> 4), idesc_dq,
+                  kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(&ds_free[pend_i & 1]);
+        if (pend_last) umma_commit(&kv_empty[pend_kb]);
+        pend_i = -1;
+      };
+      int it = 0, i = 0, j = 0;
+      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+        BwdItem t;
+        bwd_item(w, p, &t);
+        if (t.nsteps == 0) continue;
+        const int kb = it & 1;
+        ok = mbar_wait(&kv_full[kb], (it >> 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        uint32_t r0[32], r1[32];
-        tmem_ld32_async(tmem + lane_base + tDQ, r0);
-        tmem_ld32_async(tmem + lane_base + tDQ + 32, r1);
-        tmem_ld_wait();
-        reg_fence(r0);
-        reg_fence(r1);
-        tc_fence_before();
-        mbar_arrive(dq_empty);
-        if (leader) bulk_wait_group_read0();  // the previous reduce has read the staging tile
-        asm volatile("bar.sync 2, 128;" ::: "memory");
+        const uint64_t kdesc = sw128_desc(sbase + BwdSmem::kK + kb * kTile16, 16, 1024);
+        const uint64_t vdesc = sw128_desc(sbase + BwdSmem::kV + kb * kTile16, 16, 1024);
+        int step = 0;
+        for (int ri = 0; ri < t.nr && ok; ++ri)
+          for (int s = t.rg[ri].lo; s < t.rg[ri].hi && ok; s += kBwdBQ, ++i, ++step) {
+            const int st = i % kBwdStages;
+            ok = mbar_wait(&qd_full[st], (i / kBwdStages) & 1);
+            if (!ok) break;
+            tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          *reinterpret_cast<uint4*>(stage + sw128_offset(row, c)) =
-              make_uint4(r0[4 * c], r0[4 * c + 1], r0[4 * c + 2], r0[4 * c + 3]);
-          *reinterpret_cast<uint4*>(stage + kTile16 + sw128_offset(row, c)) =
-              make_uint4(r1[4 * c], r1[4 * c + 1], r1[4 * c + 2], r1[4 * c + 3]);
+            for (int h = 0; h < 2; ++h, ++j) {
+              const uint32_t qa = sbase + BwdSmem::kQ + st * kTile16 + h * (kTile16 / 2);
+              const uint32_t da = sbase + BwdSmem::kDO + st * kTile16 + h * (kTile16 / 2);
+              const uint64_t qdesc = sw128_desc(qa, 16, 1024);
+              const uint64_t dodesc = sw128_desc(da, 16, 1024);
+              const uint32_t tbuf = tmem + h * 128;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_ss(tbuf, kdesc + kk * 2, qdesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                umma_ss(tbuf + 64, vdesc + kk * 2, dodesc + kk * 2, idesc_s, kk > 0 ? 1u : 0u);
+              umma_commit(&s_full[h]);
+              if (pend_i >= 0) issue_dq();
+              if (ok && prev.j >= 0) finish(prev);
+              prev = Half{j, st, it, step == 0 && h == 0, step == t.nsteps - 1 && h == 1};
+              if (!ok) break;
+            }
+          }
+        ++it;
+      }
+      if (ok && prev.j >= 0) finish(prev);
+      if (ok && pend_i >= 0) issue_dq();
+    }
+    __syncwarp();
+  } else if (warp >= 16) {
+    // ---------------- dQ reducer and dV/dK writer: thread = row of a 128-row tile ----------
+    // dQ_i goes from TMEM to a swizzled shared-memory box (32 fp32 columns at a time) and from
+    // there into the fp32 accumulator by TMA reduce-adds, so the additions run in L2 without
+    // occupying this SM's load/store path. After an item's last dQ, the same box carries its
+    // dV and then its dK tile (64 16-bit columns) out with TMA stores, so the element-wise
+    // warps go straight on to the next item.
+    const int row = threadIdx.x - 512;
+    const bool leader = (threadIdx.x == 512);
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint8_t* stage = smem + BwdSmem::kRed;
+    // all four reducer warps agree on `ok` (they share named barrier 2 below)
+    auto agree = [](bool v) {
+      uint32_t all;
+      asm volatile(
+          "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 2, 128, p;\n"
+          " selp.u32 %0, 1, 0, q;\n}\n"
+          : "=r"(all)
+          : "r"(static_cast<uint32_t>(v))
+          : "memory");
+      return all != 0;
+    };
+    bool ok = true;
+    int it = 0, i = 0;
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      BwdItem t;
+      bwd_item(w, p, &t);
+      if (t.nsteps == 0) {  // a key tile no query sees (cannot happen under the BD3-LM mask)
+        const long long key = t.k_start + row;
+        uint4* a = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.dv) + t.bb * p.dv_sb +
+                                            t.hh * p.dv_sh + key * p.dv_ss);
+        uint4* b = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.dk) + t.bb * p.dk_sb +
+                                            t.hh * p.dk_sh + key * p.dk_ss);
+        for (int q8 = 0; q8 < 8; ++q8) a[q8] = b[q8] = make_uint4(0, 0, 0, 0);
+        continue;
+      }
+      for (int ri = 0; ri < t.nr && ok; ++ri)
+        for (int s = t.rg[ri].lo; s < t.rg[ri].hi; s += kBwdBQ, ++i) {
+          ok = agree(mbar_wait_warp(dq_full, i & 1));
+          if (!ok) break;
+          tc_fence_after();
+          // the two 32-column halves of dQ_i go through the box in turn
+#pragma unroll
+          for (int b = 0; b < 2; ++b) {
+            if (leader) bulk_wait_group_read0();  // the previous bulk op has read the box
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            uint32_t r[32];
+            tmem_ld32_async(tmem + lane_base + tDQ + 32 * b, r);
+            tmem_ld_wait();
+            reg_fence(r);
+            if (b == 1) {
+              tc_fence_before();
+              mbar_arrive(dq_empty);
+            }
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(stage + sw128_offset(row, c)) =
+                  make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+            fence_proxy_async_smem();
+            asm volatile("bar.sync 2, 128;" ::: "memory");
+            if (leader) {
+              tma_reduce_add_2d(&tm_dqacc, stage, 32 * b, static_cast<int>(t.row0 + s));
+              bulk_commit_group();
+            }
+          }
+        }
+      // ---- this item's dV, then dK (scaled), as 16-bit tiles ----
+      if (ok) ok = agree(mbar_wait_warp(acc_done, it & 1));
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int m = 0; m < 2; ++m) {
+        if (leader) bulk_wait_group_read0();
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        const float mul = m == 0 ? 1.f : p.scale;
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t r[32];
+          tmem_ld32_async(tmem + lane_base + (m == 0 ? tDV : tDK) + 32 * c2, r);
+          tmem_ld_wait();
+          reg_fence(r);
+          if (m == 1 && c2 == 1) {  // both accumulators are in registers or staged
+            tc_fence_before();
+            mbar_arrive(acc_free);
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            *reinterpret_cast<uint4*>(stage + sw128_offset(row, 4 * c2 + c)) = make_uint4(
+                pack2<kBF16>(__uint_as_float(r[8 * c + 0]) * mul, __uint_as_float(r[8 * c + 1]) * mul),
+                pack2<kBF16>(__uint_as_float(r[8 * c + 2]) * mul, __uint_as_float(r[8 * c + 3]) * mul),
+                pack2<kBF16>(__uint_as_float(r[8 * c + 4]) * mul, __uint_as_float(r[8 * c + 5]) * mul),
+                pack2<kBF16>(__uint_as_float(r[8 * c + 6]) * mul, __uint_as_float(r[8 * c + 7]) * mul));
         }
         fence_proxy_async_smem();
         asm volatile("bar.sync 2, 128;" ::: "memory");
         if (leader) {
-          const int y = static_cast<int>(row0 + s);
-          tma_reduce_add_2d(&tm_dqacc, stage, 0, y);
-          tma_reduce_add_2d(&tm_dqacc, stage + kTile16, 32, y);
+          tma_store_4d(m == 0 ? &tm_dv : &tm_dk, stage, 0, t.k_start, t.hh, t.bb);
           bulk_commit_group();
         }
       }
-    if (leader) bulk_wait_group0();  // every reduce has landed before the CTA exits
+      ++it;
+    }
+    if (leader) bulk_wait_group0();  // every reduce and store has landed before the CTA exits
   } else {
-    // ------- element-wise: thread = key row; warpgroup g takes queries [32g, 32g+32) of
+    // ------- element-wise: thread = key row; warpgroup g takes queries [16g, 16g+16) of
     // each 64-query half-step -------
     const int g = warp >> 2;
     const int row = threadIdx.x & 127;
-    const int key = k_start + row;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
     int i = 0;
-    for (int ri = 0; ri < nr && ok; ++ri) {
-      const int rule = rg[ri].rule, shift = rg[ri].shift;
-      int qlo = -2147483647, qhi = 2147483647;  // visible query interval of this key
-      if (rule != 0)
-        dkdv_col_interval(rule, shift, key, rg[ri].lo < p.n ? 0 : p.n, p.n, p.bs, &qlo, &qhi);
-      for (int s = rg[ri].lo; s < rg[ri].hi; s += kBwdBQ, ++i) {
-        const int st = i % kBwdStages;
-        ok = mbar_wait_warp(&qd_full[st], (i / kBwdStages) & 1);  // L2 / Delta rows landed
-        if (ok && i >= 2) ok = mbar_wait_warp(&ds_free[i & 1], ((i >> 1) - 1) & 1);
-        if (!ok) break;
-        const float* vL = reinterpret_cast<const float*>(smem + BwdSmem::kVec + st * 1024);
-        const float* vD = vL + 128;
-        uint8_t* sDS = smem + BwdSmem::kDS + (i & 1) * 2 * kTile16;
-#pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          ok = mbar_wait_warp(&s_full[h], i & 1);
+    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      BwdItem t;
+      bwd_item(w, p, &t);
+      const int key = t.k_start + row;
+      for (int ri = 0; ri < t.nr && ok; ++ri) {
+        const int rule = t.rg[ri].rule, shift = t.rg[ri].shift;
+        int qlo = -2147483647, qhi = 2147483647;  // visible query interval of this key
+        if (rule != 0)
+          dkdv_col_interval(rule, shift, key, t.rg[ri].lo < p.n ? 0 : p.n, p.n, p.bs, &qlo, &qhi);
+        for (int s = t.rg[ri].lo; s < t.rg[ri].hi; s += kBwdBQ, ++i) {
+          const int st = i % kBwdStages;
+          ok = mbar_wait_warp(&qd_full[st], (i / kBwdStages) & 1);  // L2 / Delta rows landed
+          if (ok && i >= 2) ok = mbar_wait_warp(&ds_free[i & 1], ((i >> 1) - 1) & 1);
           if (!ok) break;
-          tc_fence_after();
-          const uint32_t tbuf = tmem + lane_base + h * 128 + g * 32;
-          uint32_t sr[32], dr[32];
-          tmem_ld32_async(tbuf, sr);
-          tmem_ld32_async(tbuf + 64, dr);
-          tmem_ld_wait();
-          reg_fence(sr);
-          reg_fence(dr);
-          const int c0 = h * 64 + g * 32;  // first query of this thread's columns, in the step
-          const int lo = qlo - s - c0, hi = qhi - s - c0;
-          uint32_t pk[16], dk[16];
+          const float* vL = reinterpret_cast<const float*>(smem + BwdSmem::kVec + st * 1024);
+          const float* vD = vL + 128;
+          uint8_t* sDS = smem + BwdSmem::kDS + (i & 1) * 2 * kTile16;
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            ok = mbar_wait_warp(&s_full[h], i & 1);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t tbuf = tmem + lane_base + h * 128 + g * 16;
+            uint32_t sr[16], dr[16];
+            tmem_ld16_async(tbuf, sr);
+            tmem_ld16_async(tbuf + 64, dr);
+            tmem_ld_wait();
+            reg_fence(sr);
+            reg_fence(dr);
+            const int c0 = h * 64 + g * 16;  // first query of this thread's columns, in the step
+            const int lo = qlo - s - c0, hi = qhi - s - c0;
+            uint32_t pk[8], dk[8];
 #pragma unroll
-          for (int e4 = 0; e4 < 8; ++e4) {
-            const float4 l4 = *reinterpret_cast<const float4*>(vL + c0 + 4 * e4);
-            const float4 d4 = *reinterpret_cast<const float4*>(vD + c0 + 4 * e4);
-            const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-            float pv[4], dsv[4];
+            for (int e4 = 0; e4 < 4; ++e4) {
+              const float4 l4 = *reinterpret_cast<const float4*>(vL + c0 + 4 * e4);
+              const float4 d4 = *reinterpret_cast<const float4*>(vD + c0 + 4 * e4);
+              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+              float pv[4], dsv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int col = 4 * e4 + e;
-              float pe = ex2(fmaf(__uint_as_float(sr[col]), p.scale_log2, -lv[e]));
-              if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
-              pv[e] = pe;
-              dsv[e] = pe * (__uint_as_float(dr[col]) - dv4[e]);
+              for (int e = 0; e < 4; ++e) {
+                const int col = 4 * e4 + e;
+                float pe = ex2(fmaf(__uint_as_float(sr[col]), p.scale_log2, -lv[e]));
+                if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
+                pv[e] = pe;
+                dsv[e] = pe * (__uint_as_float(dr[col]) - dv4[e]);
+              }
+              pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
+              pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
+              dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
+              dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
             }
-            pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
-            pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
-            dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
-            dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
-          }
-          tmem_st16(tbuf, pk);        // P^T over this thread's own (already read) S^T columns
-          tmem_st16(tbuf + 64, dk);   // dS^T likewise over dP^T
-          // dS row for the dQ MMA: queries [32g, 32g+32) of half h are 16-byte chunks 4g..4g+3
+            tmem_st8(tbuf, pk);        // P^T over this thread's own (already read) S^T columns
+            tmem_st8(tbuf + 64, dk);   // dS^T likewise over dP^T
+            // dS row for the dQ MMA: queries [16g, 16g+16) of half h are 16-byte chunks 2g, 2g+1
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch)
-            *reinterpret_cast<uint4*>(sDS + h * kTile16 + sw128_offset(row, 4 * g + ch)) =
-                make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
-          tmem_st_wait();
-          fence_proxy_async_smem();
-          tc_fence_before();
-          mbar_arrive(&p_full[h]);
+            for (int ch = 0; ch < 2; ++ch)
+              *reinterpret_cast<uint4*>(sDS + h * kTile16 + sw128_offset(row, 2 * g + ch)) =
+                  make_uint4(dk[4 * ch], dk[4 * ch + 1], dk[4 * ch + 2], dk[4 * ch + 3]);
+            tmem_st_wait();
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(&p_full[h]);
+          }
         }
-      }
-    }
-    if (ok) ok = mbar_wait_warp(acc_done, 0);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      // warpgroup 0 writes dV, warpgroup 1 writes dK (accumulator lanes are keys)
-      uint8_t* dst = g == 0 ? reinterpret_cast<uint8_t*>(p.dv) +
-                                  2 * (bb * p.dv_sb + hh * p.dv_sh + static_cast<long long>(key) * p.dv_ss)
-                            : reinterpret_cast<uint8_t*>(p.dk) +
-                                  2 * (bb * p.dk_sb + hh * p.dk_sh + static_cast<long long>(key) * p.dk_ss);
-      if (i > 0) {
-        store_row64<kBF16>(tmem + lane_base + (g == 0 ? tDV : tDK), dst, g == 0 ? 1.f : p.scale);
-      } else {  // a key tile no query sees (cannot happen under the BD3-LM mask)
-        uint4* a = reinterpret_cast<uint4*>(dst);
-        for (int t = 0; t < 8; ++t) a[t] = make_uint4(0, 0, 0, 0);
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 13) {
+  if (warp == 21) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }

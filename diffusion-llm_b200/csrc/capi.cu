@@ -331,6 +331,9 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   if ((rc = make_map(&tk, k, dtype, S, H, B, strides + 3, 128, "k")) != BD3_OK) return rc;
   if ((rc = make_map(&tv, v, dtype, S, H, B, strides + 6, 128, "v")) != BD3_OK) return rc;
   if ((rc = make_map(&tdo, dout, dtype, S, H, B, strides + 12, 128, "dout")) != BD3_OK) return rc;
+  CUtensorMap tdk, tdv;
+  if ((rc = make_map(&tdk, dk, dtype, S, H, B, strides + 18, 128, "dk")) != BD3_OK) return rc;
+  if ((rc = make_map(&tdv, dv, dtype, S, H, B, strides + 21, 128, "dv")) != BD3_OK) return rc;
   const void* ptrs[5] = {o, dout, dq, dk, dv};
   const int idx[5] = {9, 12, 15, 18, 21};
   const char* names[5] = {"o", "dout", "dq", "dk", "dv"};
@@ -374,6 +377,7 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   p.n = static_cast<int>(n);
   p.bs = static_cast<int>(block_size);
   p.num_tiles = static_cast<int>(S / bd3::kBwdBKV);
+  p.num_bh = static_cast<int>(B * H);
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -385,12 +389,16 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
     else bd3::bwd_prep_kernel<false><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
   }
   if ((rc = check_launch("bwd_prep_kernel launch")) != BD3_OK) return rc;
-  const unsigned grid = static_cast<unsigned>(B * H * p.num_tiles);
+  const int64_t items = B * H * p.num_tiles;
+  if (items > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "too many key tiles");
+  int sms = 148;
+  if ((rc = current_device_sms(&sms)) != BD3_OK) return rc;
+  const unsigned grid = static_cast<unsigned>(items < sms ? items : sms);  // persistent
   auto fused = bf ? bd3::bwd_fused_kernel<true> : bd3::bwd_fused_kernel<false>;
   if ((rc = set_smem(fused, bd3::BwdSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
   {
     ProfScope ps(kPfDkdv, st);
-    fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, tdqa, p);
+    fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, tdqa, tdk, tdv, p);
   }
   if ((rc = check_launch("bwd_fused_kernel launch")) != BD3_OK) return rc;
   {

@@ -214,6 +214,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 // The same loads without the wait, so several can be in flight: call tmem_ld_wait() and then
 // reg_fence() on the destination registers before reading them (the fence makes every later
 // use of the registers depend on an instruction that follows the wait).
+__device__ __forceinline__ void tmem_ld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15}, [%16];\n"
+      : BD3_R8(0), BD3_R8(8)
+      : "r"(taddr)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -233,6 +241,12 @@ __device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 #undef BD3_R8
 #define BD3_W8(i) "r"(r[i]), "r"(r[i + 1]), "r"(r[i + 2]), "r"(r[i + 3]), "r"(r[i + 4]), \
                   "r"(r[i + 5]), "r"(r[i + 6]), "r"(r[i + 7])
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(
+                   taddr),
+               BD3_W8(0)
+               : "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
@@ -259,6 +273,50 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// max of three floats in one instruction (sm_100)
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Max over 64 registers as a tree of three-input maxes (depth 4, 32 instructions).
+__device__ __forceinline__ float max64(const float (&x)[64]) {
+  float m[22], n[8];
+#pragma unroll
+  for (int i = 0; i < 21; ++i) m[i] = max3(x[3 * i], x[3 * i + 1], x[3 * i + 2]);
+  m[21] = x[63];
+#pragma unroll
+  for (int i = 0; i < 7; ++i) n[i] = max3(m[3 * i], m[3 * i + 1], m[3 * i + 2]);
+  n[7] = m[21];
+  return max3(max3(n[0], n[1], n[2]), max3(n[3], n[4], n[5]), fmaxf(n[6], n[7]));
+}
+
+// 2^t for two arguments on the FMA pipe instead of the MUFU unit (which the softmax saturates).
+// Range reduction after Cody and Waite: t = j + f with j = floor(t) and f in [0, 1), so
+// 2^t = 2^j * 2^f; 2^j is added to the exponent field and 2^f is a cubic
+// p(f) = 1 + f (c1 + f (c2 + f c3)). The coefficients minimise the maximum relative error on
+// [0, 1) (Lawson's iteratively reweighted least squares, fit_exp2.py beside this file):
+// 8.6e-5, under half an ulp of bf16 and fp16 (the P operand's types). The floor comes from
+// adding 1.5 * 2^23 with rounding toward -inf, which leaves floor(t) in the low mantissa bits.
+// t is clamped to -127 first: there j = -127 and p(0) = 1, so the result's bits are exactly 0
+// (+0.0, matching ex2.approx.ftz for -inf). The callers keep t <= 8.
+__device__ __forceinline__ float2 exp2_fma2(float2 t) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC1 = 0.6951168179512024f, kC2 = 0.22764484584331512f,
+                  kC3 = 0.07706718146800995f;
+  t.x = fmaxf(t.x, -127.f);
+  t.y = fmaxf(t.y, -127.f);
+  const float2 y = __fadd2_rd(t, make_float2(kMagic, kMagic));
+  const float2 jf = __fadd2_rn(y, make_float2(-kMagic, -kMagic));
+  const float2 f = __ffma2_rn(jf, make_float2(-1.f, -1.f), t);
+  float2 p = __ffma2_rn(f, make_float2(kC3, kC3), make_float2(kC2, kC2));
+  p = __ffma2_rn(f, p, make_float2(kC1, kC1));
+  p = __ffma2_rn(f, p, make_float2(1.f, 1.f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(y.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(y.y) << 23)));
+}
+
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (kBF16) {

@@ -168,3 +168,24 @@ extern "C" __attribute__((visibility("default"))) int bd3diag_umma_selftest(cons
       ta, tb, tv, ty, static_cast<const uint16_t*>(X), S, O, C);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
+
+// exp2_fma2 (the FMA-pipe exponential of the forward softmax) and ex2.approx on the same
+// arguments, for the error-bound test.
+__global__ void diag_exp2_kernel(const float* t, float* poly, float* mufu, int n) {
+  const int i = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (i + 1 >= n) return;
+  const float2 e = bd3::exp2_fma2(make_float2(t[i], t[i + 1]));
+  poly[i] = e.x;
+  poly[i + 1] = e.y;
+  mufu[i] = bd3::ex2(t[i]);
+  mufu[i + 1] = bd3::ex2(t[i + 1]);
+}
+
+extern "C" __attribute__((visibility("default"))) int bd3diag_exp2(const float* t, float* poly,
+                                                                  float* mufu, int n,
+                                                                  void* stream) {
+  if (n <= 0 || n % 2) return 1;
+  const int threads = 256, blocks = (n / 2 + threads - 1) / threads;
+  diag_exp2_kernel<<<blocks, threads, 0, static_cast<cudaStream_t>(stream)>>>(t, poly, mufu, n);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
