@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ---------------- dQ reducer and dV/dK writer: thread = row of a 128-row tile ----------
     // dQ_i goes from TMEM to a swizzled shared-memory box (32 fp32 columns at a time) and from
     // there into the fp32 accumulator by TMA reduce-adds, so the additions run in L2 without
-    // occupying this SM's load/store path. After an item's last dQ, the same box carries its
+    // occupying this SM's load/store path. Before an item's last dQ, the same box carries its
     // dV and then its dK tile (64 16-bit columns) out with TMA stores, so the element-wise
     // warps go straight on to the next item.
     const int row = threadIdx.x - 512;
@@ -448,8 +448,47 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int q8 = 0; q8 < 8; ++q8) a[q8] = b[q8] = make_uint4(0, 0, 0, 0);
         continue;
       }
+      int step = 0;
       for (int ri = 0; ri < t.nr && ok; ++ri)
-        for (int s = t.rg[ri].lo; s < t.rg[ri].hi; s += kBwdBQ, ++i) {
+        for (int s = t.rg[ri].lo; s < t.rg[ri].hi; s += kBwdBQ, ++i, ++step) {
+          if (step == t.nsteps - 1) {
+            // ---- this item's dV, then dK (scaled), as 16-bit tiles. Read out as soon as the
+            // item's last dV/dK MMAs are done, before its last dQ (which queues behind the
+            // next item's first S^T/dP^T), so the next item's first dV/dK MMAs need not wait.
+            ok = agree(mbar_wait_warp(acc_done, it & 1));
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int m = 0; m < 2; ++m) {
+              if (leader) bulk_wait_group_read0();  // the previous bulk op has read the box
+              asm volatile("bar.sync 2, 128;" ::: "memory");
+              const float mul = m == 0 ? 1.f : p.scale;
+#pragma unroll
+              for (int c2 = 0; c2 < 2; ++c2) {
+                uint32_t r[32];
+                tmem_ld32_async(tmem + lane_base + (m == 0 ? tDV : tDK) + 32 * c2, r);
+                tmem_ld_wait();
+                reg_fence(r);
+                if (m == 1 && c2 == 1) {  // both accumulators have been read
+                  tc_fence_before();
+                  mbar_arrive(acc_free);
+                }
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                  *reinterpret_cast<uint4*>(stage + sw128_offset(row, 4 * c2 + c)) = make_uint4(
+                      pack2<kBF16>(__uint_as_float(r[8 * c + 0]) * mul, __uint_as_float(r[8 * c + 1]) * mul),
+                      pack2<kBF16>(__uint_as_float(r[8 * c + 2]) * mul, __uint_as_float(r[8 * c + 3]) * mul),
+                      pack2<kBF16>(__uint_as_float(r[8 * c + 4]) * mul, __uint_as_float(r[8 * c + 5]) * mul),
+                      pack2<kBF16>(__uint_as_float(r[8 * c + 6]) * mul, __uint_as_float(r[8 * c + 7]) * mul));
+              }
+              fence_proxy_async_smem();
+              asm volatile("bar.sync 2, 128;" ::: "memory");
+              if (leader) {
+                tma_store_4d(m == 0 ? &tm_dv : &tm_dk, stage, 0, t.k_start, t.hh, t.bb);
+                bulk_commit_group();
+              }
+            }
+          }
           ok = agree(mbar_wait_warp(dq_full, i & 1));
           if (!ok) break;
           tc_fence_after();
@@ -478,40 +517,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
         }
-      // ---- this item's dV, then dK (scaled), as 16-bit tiles ----
-      if (ok) ok = agree(mbar_wait_warp(acc_done, it & 1));
-      if (!ok) break;
-      tc_fence_after();
-#pragma unroll 1
-      for (int m = 0; m < 2; ++m) {
-        if (leader) bulk_wait_group_read0();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        const float mul = m == 0 ? 1.f : p.scale;
-#pragma unroll
-        for (int c2 = 0; c2 < 2; ++c2) {
-          uint32_t r[32];
-          tmem_ld32_async(tmem + lane_base + (m == 0 ? tDV : tDK) + 32 * c2, r);
-          tmem_ld_wait();
-          reg_fence(r);
-          if (m == 1 && c2 == 1) {  // both accumulators are in registers or staged
-            tc_fence_before();
-            mbar_arrive(acc_free);
-          }
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(stage + sw128_offset(row, 4 * c2 + c)) = make_uint4(
-                pack2<kBF16>(__uint_as_float(r[8 * c + 0]) * mul, __uint_as_float(r[8 * c + 1]) * mul),
-                pack2<kBF16>(__uint_as_float(r[8 * c + 2]) * mul, __uint_as_float(r[8 * c + 3]) * mul),
-                pack2<kBF16>(__uint_as_float(r[8 * c + 4]) * mul, __uint_as_float(r[8 * c + 5]) * mul),
-                pack2<kBF16>(__uint_as_float(r[8 * c + 6]) * mul, __uint_as_float(r[8 * c + 7]) * mul));
-        }
-        fence_proxy_async_smem();
-        asm volatile("bar.sync 2, 128;" ::: "memory");
-        if (leader) {
-          tma_store_4d(m == 0 ? &tm_dv : &tm_dk, stage, 0, t.k_start, t.hh, t.bb);
-          bulk_commit_group();
-        }
-      }
       ++it;
     }
     if (leader) bulk_wait_group0();  // every reduce and store has landed before the CTA exits
