@@ -38,6 +38,13 @@ METRIC = "BD3-LM attn fwd+bwd TFLOP/s (useful FLOPs, bwd = 2.5x fwd)"
 UNIT = "TFLOP/s"
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each training
+# kernel on the C2 workload at B=8, from one `ncu --set full` capture (summarised in
+# profiles/bwd_fused_c2.md and profiles/attn_fwd_c2.md). The work is B x H independent
+# (batch, head) slices, so the traffic scales with B.
+NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 310_583_552, "attn_fwd": 83_232_000}
+
+
 def nnz(n: int, bs: int) -> int:
     """Visible (query, key) pairs of block_diff_mask(n, bs) when bs divides n."""
     return n * n + n * bs
@@ -379,7 +386,9 @@ def run_ours(args) -> None:
                        "l2": "256 MiB buffer written before every step (outside the events)"},
             "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 2),
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": round(achieved / peaks["bf16_tflops"], 4), "traffic": None,
+                         "frac": round(achieved / peaks["bf16_tflops"], 4),
+                         "traffic": round(NCU_TRAFFIC_BYTES_B8[dom] * B / 8),
+                         "traffic_unit": "DRAM bytes per launch (ncu capture, scaled by B/8)",
                          "peak_source": peaks["source"] + " burst bf16"},
             "e2e": {"value": round(e2e_val, 3), "unit": UNIT,
                     "h2d_bytes_per_step": 4 * tensor_bytes, "d2h_bytes_per_step": 3 * tensor_bytes},
