@@ -551,33 +551,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (!ok) break;
             tc_fence_after();
             const uint32_t tbuf = tmem + lane_base + h * 128 + g * 16;
-            uint32_t sr[16], dr[16];
-            tmem_ld16_async(tbuf, sr);
-            tmem_ld16_async(tbuf + 64, dr);
-            tmem_ld_wait();
-            reg_fence(sr);
-            reg_fence(dr);
             const int c0 = h * 64 + g * 16;  // first query of this thread's columns, in the step
             const int lo = qlo - s - c0, hi = qhi - s - c0;
+            // a warp whose 32 keys see none of its 16 queries writes P^T = dS^T = 0 and skips
+            // the exponentials (rule != 0 steps only)
+            const bool skip = rule != 0 && __all_sync(0xffffffffu, hi <= 0 || lo >= 16 || hi <= lo);
             uint32_t pk[8], dk[8];
+            if (skip) {
 #pragma unroll
-            for (int e4 = 0; e4 < 4; ++e4) {
-              const float4 l4 = *reinterpret_cast<const float4*>(vL + c0 + 4 * e4);
-              const float4 d4 = *reinterpret_cast<const float4*>(vD + c0 + 4 * e4);
-              const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
-              float pv[4], dsv[4];
+              for (int e = 0; e < 8; ++e) pk[e] = dk[e] = 0u;
+            } else {
+              uint32_t sr[16], dr[16];
+              tmem_ld16_async(tbuf, sr);
+              tmem_ld16_async(tbuf + 64, dr);
+              tmem_ld_wait();
+              reg_fence(sr);
+              reg_fence(dr);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int col = 4 * e4 + e;
-                float pe = ex2(fmaf(__uint_as_float(sr[col]), p.scale_log2, -lv[e]));
-                if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
-                pv[e] = pe;
-                dsv[e] = pe * (__uint_as_float(dr[col]) - dv4[e]);
+              for (int e4 = 0; e4 < 4; ++e4) {
+                const float4 l4 = *reinterpret_cast<const float4*>(vL + c0 + 4 * e4);
+                const float4 d4 = *reinterpret_cast<const float4*>(vD + c0 + 4 * e4);
+                const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+                float pv[4], dsv[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int col = 4 * e4 + e;
+                  float pe = ex2(fmaf(__uint_as_float(sr[col]), p.scale_log2, -lv[e]));
+                  if (rule != 0 && (col < lo || col >= hi)) pe = 0.f;
+                  pv[e] = pe;
+                  dsv[e] = pe * (__uint_as_float(dr[col]) - dv4[e]);
+                }
+                pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
+                pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
+                dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
+                dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
               }
-              pk[2 * e4] = pack2<kBF16>(pv[0], pv[1]);
-              pk[2 * e4 + 1] = pack2<kBF16>(pv[2], pv[3]);
-              dk[2 * e4] = pack2<kBF16>(dsv[0], dsv[1]);
-              dk[2 * e4 + 1] = pack2<kBF16>(dsv[2], dsv[3]);
             }
             tmem_st8(tbuf, pk);        // P^T over this thread's own (already read) S^T columns
             tmem_st8(tbuf + 64, dk);   // dS^T likewise over dP^T

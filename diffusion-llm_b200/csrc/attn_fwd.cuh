@@ -318,56 +318,66 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
           if (!ok) break;
           tc_fence_after();
           const uint32_t tS = tmem + lane_base + b * 128 + g * 64;
-          float x[64];
-          {
-            uint32_t r[2][32];
-            tmem_ld32_async(tS, r[0]);
-            tmem_ld32_async(tS + 32, r[1]);
-            tmem_ld_wait();
-#pragma unroll
-            for (int c2 = 0; c2 < 2; ++c2) {
-              reg_fence(r[c2]);
-#pragma unroll
-              for (int i = 0; i < 32; ++i) x[c2 * 32 + i] = __uint_as_float(r[c2][i]);
-            }
-          }
-          if (rule != 0) {
-            const int lo = vlo - s - g * 64, hi = vhi - s - g * 64;
-#pragma unroll
-            for (int c = 0; c < 64; ++c)
-              if (c < lo || c >= hi) x[c] = -INFINITY;
-          }
-          const float mx = max64(x) * p.scale_log2;
-          const float m_new = fmaxf(m_run, mx);
-          float alpha = 1.f;
+          // this row's visible columns within this warpgroup's 64 (rule != 0 tiles only); a
+          // warp whose 32 rows see none of them writes P = 0 and skips the exponentials
+          const int lo = vlo - s - g * 64, hi = vhi - s - g * 64;
+          const bool skip = rule != 0 && __all_sync(0xffffffffu, hi <= 0 || lo >= 64 || hi <= lo);
+          float alpha = 1.f, sum = 0.f;
           bool rescale = false;
-          if (m_new - m_run > kRescaleLog2) {  // false for NaN (-inf - -inf)
-            alpha = ex2(m_run - m_new);        // 0 when m_run = -inf
-            rescale = (j > 0);
-            m_run = m_new;
-          }
-          const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-          // P = 2^(x * scale - m): kFwdPolyPairs of the 32 column pairs on the FMA pipe, the
-          // rest on MUFU, so that the two units share the exponentials
-          const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
-          const float2 nm2 = make_float2(-m_use, -m_use);
-          float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
-                           make_float2(0.f, 0.f)};
-          uint32_t pk[32];
+          if (skip) {
+            uint32_t zero[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float2 t = __ffma2_rn(make_float2(x[2 * i], x[2 * i + 1]), sc2, nm2);
-            float2 e;
-            if ((i * kFwdPolyPairs) / 32 != ((i + 1) * kFwdPolyPairs) / 32)
-              e = exp2_fma2(t);
-            else
-              e = make_float2(ex2(t.x), ex2(t.y));
-            acc[i & 3] = __fadd2_rn(acc[i & 3], e);
-            pk[i] = pack2<kBF16>(e.x, e.y);
+            for (int i = 0; i < 32; ++i) zero[i] = 0u;
+            tmem_st32(tS, zero);
+          } else {
+            float x[64];
+            {
+              uint32_t r[2][32];
+              tmem_ld32_async(tS, r[0]);
+              tmem_ld32_async(tS + 32, r[1]);
+              tmem_ld_wait();
+#pragma unroll
+              for (int c2 = 0; c2 < 2; ++c2) {
+                reg_fence(r[c2]);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) x[c2 * 32 + i] = __uint_as_float(r[c2][i]);
+              }
+            }
+            if (rule != 0) {
+#pragma unroll
+              for (int c = 0; c < 64; ++c)
+                if (c < lo || c >= hi) x[c] = -INFINITY;
+            }
+            const float mx = max64(x) * p.scale_log2;
+            const float m_new = fmaxf(m_run, mx);
+            if (m_new - m_run > kRescaleLog2) {  // false for NaN (-inf - -inf)
+              alpha = ex2(m_run - m_new);        // 0 when m_run = -inf
+              rescale = (j > 0);
+              m_run = m_new;
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+            // P = 2^(x * scale - m): kFwdPolyPairs of the 32 column pairs on the FMA pipe, the
+            // rest on MUFU, so that the two units share the exponentials
+            const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+            const float2 nm2 = make_float2(-m_use, -m_use);
+            float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
+                             make_float2(0.f, 0.f)};
+            uint32_t pk[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float2 t = __ffma2_rn(make_float2(x[2 * i], x[2 * i + 1]), sc2, nm2);
+              float2 e;
+              if ((i * kFwdPolyPairs) / 32 != ((i + 1) * kFwdPolyPairs) / 32)
+                e = exp2_fma2(t);
+              else
+                e = make_float2(ex2(t.x), ex2(t.y));
+              acc[i & 3] = __fadd2_rn(acc[i & 3], e);
+              pk[i] = pack2<kBF16>(e.x, e.y);
+            }
+            const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
+            sum = a01.x + a01.y;
+            tmem_st32(tS, pk);  // P_g over this warpgroup's own (already read) S columns
           }
-          const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
-          const float sum = a01.x + a01.y;
-          tmem_st32(tS, pk);  // P_g over this warpgroup's own (already read) S columns
           l_run = l_run * alpha + sum;
           tmem_st_wait();
           if (j > 0) {
