@@ -92,16 +92,19 @@ class ClockSampler:
         self.max_mhz = None
         self.error = None
 
-    def _run(self):
+    def _sample(self) -> bool:
         import pynvml
-        while not self.stop.is_set():
-            try:
-                sm = pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-                rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((float(sm), int(rs)))
-            except Exception as e:  # keep the timed run going; report the error
-                self.error = repr(e)
-                return
+        try:
+            sm = pynvml.nvmlDeviceGetClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            self.samples.append((float(sm), int(rs)))
+            return True
+        except Exception as e:  # keep the timed run going; report the error
+            self.error = repr(e)
+            return False
+
+    def _run(self):
+        while not self.stop.is_set() and self._sample():
             time.sleep(0.002)
 
     def __enter__(self):
@@ -111,6 +114,11 @@ class ClockSampler:
             pynvml.nvmlInit()
             self.h = pynvml.nvmlDeviceGetHandleByPciBusId(nvml_bus_id(self.device))
             self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self._sample()  # one sample at the start of the region, whatever the thread gets
+            # the main thread launches kernels and waits on NCCL while holding the GIL for
+            # long stretches: let the sampler in every 0.5 ms
+            self.switch = sys.getswitchinterval()
+            sys.setswitchinterval(0.0005)
             self.stop = threading.Event()
             self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
@@ -123,6 +131,8 @@ class ClockSampler:
         if getattr(self, "thread", None) is not None:
             self.stop.set()
             self.thread.join(timeout=2)
+            sys.setswitchinterval(self.switch)
+            self._sample()  # and one at its end
 
     def summary(self) -> dict:
         import pynvml
