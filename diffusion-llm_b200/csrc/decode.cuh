@@ -79,20 +79,33 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
   }
 }
 
-// Key tile `t` of this CTA's list: its first key, or -1 past the end.
+constexpr int kDecLiveCache = 256;  // live entries of a split cached in shared memory
+
+// Key tile `t` of this CTA's list: its first key, or -1 past the end. Live mode reads the
+// split's block indices from `live` (the first kDecLiveCache entries, staged in shared memory
+// by the producer warp; `n_live` = entries of this split) and any beyond from global memory.
 template <bool kLive>
 __device__ __forceinline__ int dec_tile_key(const DecParams& p, int bh, int split, int t,
-                                            int n_tiles) {
+                                            int n_tiles, const int* live, int n_live) {
   if constexpr (!kLive) {
     const int g = split * p.tiles_per_split + t;
     return (t < p.tiles_per_split && g < n_tiles) ? g * kDecBN : -1;
   } else {
     const int per_block = p.kv_block / kDecBN;
-    const int e = split * p.tiles_per_split + t / per_block;
-    if (t / per_block >= p.tiles_per_split || e >= p.live_cnt[bh]) return -1;
-    return p.live_idx[static_cast<long long>(bh) * p.live_stride + e] * p.kv_block +
-           (t % per_block) * kDecBN;
+    const int e = t / per_block;
+    if (e >= n_live) return -1;
+    const int blk = e < kDecLiveCache
+                        ? live[e]
+                        : p.live_idx[static_cast<long long>(bh) * p.live_stride +
+                                     split * p.tiles_per_split + e];
+    return blk * p.kv_block + (t % per_block) * kDecBN;
   }
+}
+
+// Live entries of this split: min(tiles_per_split, live_cnt - first entry), at least 0.
+__device__ __forceinline__ int dec_split_entries(const DecParams& p, int bh, int split) {
+  const int left = p.live_cnt[bh] - split * p.tiles_per_split;
+  return left < 0 ? 0 : (left < p.tiles_per_split ? left : p.tiles_per_split);
 }
 
 struct DecSmem {
@@ -100,7 +113,8 @@ struct DecSmem {
   static constexpr uint32_t kStage = 8192;                     // K then V, per stage
   static constexpr uint32_t kBar = kStage + kDecStages * 2 * kDecTile;
   static constexpr uint32_t kNumBars = 1 + 2 * kDecStages;     // q_full, full[S], empty[S]
-  static constexpr uint32_t kBytes = kBar + kNumBars * 8;
+  static constexpr uint32_t kLive = kBar + kNumBars * 8;       // [kDecLiveCache] block indices
+  static constexpr uint32_t kBytes = kLive + kDecLiveCache * 4;
   static constexpr uint32_t kAlloc = kBytes + 1024;
 };
 
@@ -138,14 +152,26 @@ __global__ void __launch_bounds__(kDecThreads)
   }
   __syncthreads();
 
+  int* live = reinterpret_cast<int*>(smem + DecSmem::kLive);
+  const int n_live = kLive ? dec_split_entries(p, bh, split) : 0;
   if (warp == 4) {
     // ---------------- producer ----------------
+    if constexpr (kLive) {
+      // stage this split's block indices in shared memory with coalesced loads, so no tile
+      // waits on a dependent global read (the consumers see them after q_full completes)
+      const int* src = p.live_idx + static_cast<long long>(bh) * p.live_stride +
+                       split * p.tiles_per_split;
+      const int n_cache = n_live < kDecLiveCache ? n_live : kDecLiveCache;
+      for (int e = lane; e < n_cache; e += 32) live[e] = src[e];
+      __threadfence_block();
+      __syncwarp();
+    }
     if (elect_one()) {
       mbar_expect_tx(q_full, kMB * 16 * 128);
       tma_load_4d(&tm_q, q_full, smem + DecSmem::kQ, 0, row0, hh, bb);
       bool ok = true;
       for (int t = 0;; ++t) {
-        const int key = dec_tile_key<kLive>(p, bh, split, t, n_tiles);
+        const int key = dec_tile_key<kLive>(p, bh, split, t, n_tiles, live, n_live);
         if (key < 0) break;
         const int st = t % kDecStages;
         if (t >= kDecStages) ok = mbar_wait(&empty[st], ((t / kDecStages) - 1) & 1);
@@ -194,7 +220,7 @@ __global__ void __launch_bounds__(kDecThreads)
   const int full_all = dec_row_hi(p, row0);  // keys below this are seen by every row here
 
   for (int t = 0; ok; ++t) {
-    const int key = dec_tile_key<kLive>(p, bh, split, t, n_tiles);
+    const int key = dec_tile_key<kLive>(p, bh, split, t, n_tiles, live, n_live);
     if (key < 0) break;
     const int st = t % kDecStages;
     ok = mbar_wait_warp(&full[st], (t / kDecStages) & 1);

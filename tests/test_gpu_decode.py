@@ -148,3 +148,35 @@ def test_non_contiguous_cache_views():
     assert_device_ok()
     ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(16, 2048, 16))
     assert_close("O", o, ref, O_TOL)
+
+
+def test_live_blocks_long_list_single_split():
+    """One split over a 300-entry live list, through the C ABI: the kernel stages the first
+    256 entries of a split in shared memory and reads the rest from global memory."""
+    import ctypes
+    from bd3attn._lib import LIB
+    B, H, q_len, kv_len, kv_block, bs, n_live = 1, 2, 16, 64 * 400, 64, 16, 300
+    q, k, v = qkv(12, B, H, q_len, kv_len)
+    rng = np.random.default_rng(3)
+    nb = kv_len // kv_block
+    live = np.stack([np.sort(np.concatenate([rng.choice(nb - 1, n_live - 1, replace=False),
+                                             [nb - 1]])) for _ in range(B * H)])
+    live = live.reshape(B, H, n_live).astype(np.int32)
+    cnt = np.full((B, H), n_live, dtype=np.int32)
+    qd, kd, vd = q.cuda(), k.cuda(), v.cuda()
+    ld, cd = torch.from_numpy(live).cuda(), torch.from_numpy(cnt).cuda()
+    o = torch.empty_like(qd)
+    st = []
+    for t in (qd, kd, vd, o):
+        st += [t.stride(0), t.stride(1), t.stride(2)]
+    rc = LIB.bd3_decode_live_blocks(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), o.data_ptr(),
+                                    None, ld.data_ptr(), cd.data_ptr(), n_live, n_live, kv_block,
+                                    B, H, q_len, kv_len, 64, (ctypes.c_int64 * 12)(*st), bs, 1,
+                                    0, 0, None, 0, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, LIB.bd3_last_error()
+    torch.cuda.synchronize()
+    assert_device_ok()
+    lists = [[live[0, h].tolist() for h in range(H)]]
+    mask = oracle.live_block_mask(lists, q_len, kv_len, kv_block, bs)
+    ref, _ = oracle.attention(q, k, v, mask)
+    assert_close("O", o, ref, O_TOL)
