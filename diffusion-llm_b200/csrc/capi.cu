@@ -639,9 +639,13 @@ int bd3_decode_live_plan(int64_t B, int64_t H, int64_t q_len, int64_t max_live,
   if (rc != BD3_OK) return rc;
   const int64_t groups = (q_len + 31) / 32;
   const int64_t per = kv_block / 64;
-  // units are live entries; each entry is `per` tiles
-  int64_t u = pick_units_per_split(B * H * groups, max_live * per, sms);
-  u = (u + per - 1) / per;
+  // units are live entries; each entry is `per` tiles. Once (batch, head) x row groups give
+  // every SM a CTA, one split per (batch, head) is fastest: the lists are short, so extra
+  // splits only add CTAs contending for the same scattered blocks plus the combine pass
+  // (measured on B=16, H=12, 32 live 64-key blocks: 26.6 us with 1 split, 29.7 with 2).
+  int64_t u = B * H * groups >= sms ? max_live
+                                    : (pick_units_per_split(B * H * groups, max_live * per, sms) +
+                                       per - 1) / per;
   const int64_t s = (max_live + u - 1) / u;
   *n_splits = s;
   *workspace_bytes = s > 1 ? static_cast<size_t>(B * H * s * q_len) * 65 * 4 : 0;
