@@ -361,24 +361,62 @@ def run_ours(args) -> None:
     f4, b4 = useful_flops(B, N_HALF, 4)
     bs4 = (f4 + b4) / (statistics.mean(ms4) * 1e-3) / 1e12
 
-    # e2e: the public autograd API with host buffers, H2D + fwd + bwd + D2H every step
+    # e2e: the public autograd API with host buffers. Every step copies its q, k, v, dO in
+    # from pinned host memory and its dQ, dK, dV out to pinned host memory, as a training
+    # input pipeline does: the device inputs are double-buffered and the copies run on their
+    # own streams, so step i+1's inputs and step i-1's gradients cross PCIe while step i
+    # computes. One timed region covers all K steps, from before the first copy in to after
+    # the last copy out; each step's working set (~250 MB) is larger than L2.
     host = [t.cpu().pin_memory() for t in (q, k, v, do)]
-    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+    outs = [[torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+            for _ in range(2)]
+    dbuf = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+    for bset in dbuf:
+        for t in bset[:3]:
+            t.requires_grad_(True)
 
-    def e2e_step():
-        qd, kd, vd, dod = (h.to(dev, non_blocking=True) for h in host)
-        qd.requires_grad_(True)
-        kd.requires_grad_(True)
-        vd.requires_grad_(True)
-        o = BlockSparseFlashAttention.apply(qd, kd, vd, BS)
-        grads = torch.autograd.grad(o, (qd, kd, vd), dod)
-        for dst, src in zip(outs, grads):
-            dst.copy_(src, non_blocking=True)
+    def e2e_run(steps: int) -> float:
+        comp = torch.cuda.current_stream()
+        h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+        ev_in = [torch.cuda.Event() for _ in range(2)]    # a slot's inputs have landed
+        ev_used = [torch.cuda.Event() for _ in range(2)]  # a slot's step has computed
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        keep = []
+        h2d.wait_stream(comp)
+        start.record(h2d)
 
-    for _ in range(2):
-        e2e_step()
+        def load(i):
+            slot = i % 2
+            if i >= 2:
+                h2d.wait_event(ev_used[slot])
+            with torch.cuda.stream(h2d), torch.no_grad():
+                for dst, src in zip(dbuf[slot], host):
+                    dst.copy_(src, non_blocking=True)
+            ev_in[slot].record(h2d)
+
+        load(0)
+        for i in range(steps):
+            if i + 1 < steps:
+                load(i + 1)
+            slot = i % 2
+            comp.wait_event(ev_in[slot])
+            qd, kd, vd, dod = dbuf[slot]
+            o = BlockSparseFlashAttention.apply(qd, kd, vd, BS)
+            grads = torch.autograd.grad(o, (qd, kd, vd), dod)
+            ev_used[slot].record(comp)
+            d2h.wait_event(ev_used[slot])
+            with torch.cuda.stream(d2h):
+                for dst, src in zip(outs[slot], grads):
+                    dst.copy_(src, non_blocking=True)
+            keep.append(grads)  # alive until the copies out are done
+        end.record(d2h)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end)
+
+    e2e_run(2)
     barrier(world)
-    e2e_ms = max_over_ranks(sum(time_steps(e2e_step, args.steps, l2)), world)
+    e2e_ms = max_over_ranks(e2e_run(args.steps), world)
     e2e_val = (fwd_f + bwd_f) * args.steps * world / (e2e_ms * 1e-3) / 1e12
     tensor_bytes = q.numel() * q.element_size()
 
@@ -411,7 +449,10 @@ def run_ours(args) -> None:
                          "traffic_unit": "DRAM bytes per launch (ncu capture, scaled by B/8)",
                          "peak_source": peaks["source"] + " burst bf16"},
             "e2e": {"value": round(e2e_val, 3), "unit": UNIT,
-                    "h2d_bytes_per_step": 4 * tensor_bytes, "d2h_bytes_per_step": 3 * tensor_bytes},
+                    "h2d_bytes_per_step": 4 * tensor_bytes, "d2h_bytes_per_step": 3 * tensor_bytes,
+                    "ms_per_step": round(e2e_ms / args.steps, 4),
+                    "timing": "one region over all steps; copies in/out on their own streams "
+                              "overlap the neighbouring steps' compute (double-buffered inputs)"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
