@@ -180,3 +180,38 @@ def test_live_blocks_long_list_single_split():
     mask = oracle.live_block_mask(lists, q_len, kv_len, kv_block, bs)
     ref, _ = oracle.attention(q, k, v, mask)
     assert_close("O", o, ref, O_TOL)
+
+
+def test_full_config3_size():
+    """BASELINE config 3 at its largest single-GPU size (B=32, H=12, q_len 16, a 64K cache
+    plus the block itself): the planned split-KV decode equals the oracle on two (b, h)
+    slices, and equals the LSE merge of two sequence-shard decodes of the same cache (a
+    size-independent consistency check over all 384 (b, h) pairs)."""
+    from bd3attn import ops
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    B, H, q_len, kv_len, bs = 32, 12, 16, 65536 + 16, 16
+    g = torch.Generator(device="cuda").manual_seed(17)
+    q = torch.randn(B, H, q_len, 64, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, H, kv_len, 64, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, H, kv_len, 64, device="cuda", generator=g).bfloat16()
+    o = split_kv_decode_attention(q, k, v, bs)
+    full, full_lse = ops.decode_raw(q, k, v, bs, out_dtype=torch.float32, return_lse=True)
+    torch.cuda.synchronize()
+    assert_device_ok()
+    sl = (slice(31, 32), slice(0, 2))
+    mask = oracle.block_causal_mask(q_len, kv_len, bs)
+    ref, ref_lse = oracle.attention(q[sl].cpu(), k[sl].cpu(), v[sl].cpu(), mask)
+    assert_close("O", o[sl], ref, O_TOL)
+    assert_close("LSE", full_lse[sl], ref_lse, LSE_TOL)
+    half = 32768  # shard edge, a multiple of the 64-key tile
+    parts, lses = [], []
+    for lo, hi in ((0, half), (half, kv_len)):
+        po, pl = ops.decode_raw(q, k[:, :, lo:hi], v[:, :, lo:hi], bs, q_pos0=kv_len - q_len,
+                                kv_pos0=lo, out_dtype=torch.float32, return_lse=True)
+        parts.append(po)
+        lses.append(pl)
+    merged, merged_lse = ops.lse_merge_raw(torch.stack(parts), torch.stack(lses), torch.float32)
+    torch.cuda.synchronize()
+    assert_device_ok()
+    assert_close("O merged vs planned", merged, full, 1e-3)
+    assert_close("LSE merged vs planned", merged_lse, full_lse, 1e-4)
