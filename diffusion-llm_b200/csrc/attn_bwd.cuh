@@ -189,7 +189,7 @@ __device__ __forceinline__ int bwd_tile_order(int t, int num_tiles) {
 __device__ __forceinline__ uint32_t half_ts_col(int kk) { return static_cast<uint32_t>(kk) * 16; }
 
 // Work item w of the persistent loop: one key tile of one (batch, head). Items are numbered
-// heaviest first (bwd_tile_order), so a round-robin over CTAs balances the steps.
+// heaviest first (bwd_tile_order), and CTAs take them in alternating rounds (persistent_item).
 struct BwdItem {
   int bb, hh, k_start, nr, nsteps;
   long long row0;  // first row of this (batch, head) in the flattened (B*H*2n) row space
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (elect_one()) {
       bool ok = true;
       int it = 0, i = 0;
-      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      for (int k = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++k)) {
         BwdItem t;
         bwd_item(w, p, &t);
         if (t.nsteps == 0) continue;
@@ -369,7 +369,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         pend_i = -1;
       };
       int it = 0, i = 0, j = 0;
-      for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+      for (int k = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++k)) {
         BwdItem t;
         bwd_item(w, p, &t);
         if (t.nsteps == 0) continue;
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     };
     bool ok = true;
     int it = 0, i = 0;
-    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+    for (int k = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++k)) {
       BwdItem t;
       bwd_item(w, p, &t);
       if (t.nsteps == 0) {  // a key tile no query sees (cannot happen under the BD3-LM mask)
@@ -528,7 +528,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     bool ok = true;
     int i = 0;
-    for (int w = blockIdx.x; w < num_items && ok; w += gridDim.x) {
+    for (int k = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++k)) {
       BwdItem t;
       bwd_item(w, p, &t);
       const int key = t.k_start + row;

@@ -185,7 +185,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     if (elect_one()) {
       bool ok = true;
       int J = 0;  // key tiles loaded so far by this CTA
-      for (int w = blockIdx.x, it = 0; w < num_items && ok; w += gridDim.x, ++it) {
+      for (int it = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++it)) {
         int bh, q_tile;
         fwd_item(w, p, kMode, &bh, &q_tile);
         const int bb = bh / p.H, hh = bh % p.H;
@@ -241,14 +241,13 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
       // One flat loop over this CTA's key tiles across its items: S(J) is issued before
       // O += P V of tile J-1, also across item boundaries, so the S buffers never drain.
       int J = 0;                 // key tiles issued so far by this CTA
-      int it = -1, w = blockIdx.x - static_cast<int>(gridDim.x), nt = 0, j = 0;
+      int it = -1, w = 0, nt = 0, j = 0;
       uint64_t qdesc = 0;
       int prev_J = -1, prev_it = 0;
       bool prev_first = false;
       while (ok) {
         if (j == nt) {  // next item (an item always has at least one key tile)
-          w += gridDim.x;
-          ++it;
+          w = persistent_item(++it);
           if (w >= num_items) break;
           int bh, q_tile;
           fwd_item(w, p, kMode, &bh, &q_tile);
@@ -291,7 +290,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1)
     const uint32_t tO = tmem + lane_base + 256 + g * 64;
     bool ok = true;
     int J = 0;  // key tiles consumed so far by this CTA
-    for (int w = blockIdx.x, it = 0; w < num_items; w += gridDim.x, ++it) {
+    for (int it = 0, w = persistent_item(0); w < num_items; w = persistent_item(++it)) {
       int bh, q_tile;
       fwd_item(w, p, kMode, &bh, &q_tile);
       const int bb = bh / p.H, hh = bh % p.H;

@@ -40,6 +40,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// Work item of this CTA's k-th turn in a persistent loop: turns are rounds of gridDim.x
+// consecutive items taken in alternating directions, so a list ordered heaviest first gives
+// each CTA one early (heavy) and one late (light) item of every pair of rounds. Increasing
+// in k for every CTA, so the first item index past the end ends the loop.
+__device__ __forceinline__ int persistent_item(int k) {
+  const int G = static_cast<int>(gridDim.x), c = static_cast<int>(blockIdx.x);
+  return k * G + ((k & 1) ? G - 1 - c : c);
+}
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31u; }
 __device__ __forceinline__ uint32_t warp_id() {
   return __shfl_sync(0xffffffffu, threadIdx.x >> 5, 0);
