@@ -42,7 +42,7 @@ UNIT = "TFLOP/s"
 # kernel on the C2 workload at B=8, from one `ncu --set full` capture (summarised in
 # profiles/bwd_fused_c2.md and profiles/attn_fwd_c2.md). The work is B x H independent
 # (batch, head) slices, so the traffic scales with B.
-NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 310_583_552, "attn_fwd": 83_232_000}
+NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 319_690_752, "attn_fwd": 82_574_336}
 
 
 def nnz(n: int, bs: int) -> int:
@@ -75,6 +75,22 @@ def nvml_bus_id(device: int) -> str:
     if not all(isinstance(x, int) for x in (dom, bus, dev)):
         raise TypeError("PCI ids are not integers")
     return f"{dom:08x}:{bus:02x}:{dev:02x}.0"
+
+
+def gpu_local_cpus(device: int):
+    """The host CPUs NVML lists as local to the GPU (its NUMA node), within this process's
+    allowed set; None when NVML does not say."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(nvml_bus_id(device))
+        words = (os.cpu_count() + 63) // 64
+        mask = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
 
 
 class ClockSampler:
@@ -259,7 +275,8 @@ def flush_l2(l2) -> None:
     back (a write-only flush leaves ~126 MB of dirty lines whose write-back the next step
     would pay for)."""
     l2.zero_()
-    torch.sum(l2.view(torch.int32))
+    torch.sum(l2.view(torch.float32))  # float32 sums in place (an int32 sum would first copy
+                                       # the buffer to int64, leaving dirty lines in L2)
 
 
 def time_steps(fn, steps: int, l2) -> list[float]:
@@ -374,10 +391,34 @@ def run_ours(args) -> None:
     # own streams, so step i+1's inputs and step i-1's gradients cross PCIe while step i
     # computes. One timed region covers all K steps, from before the first copy in to after
     # the last copy out; each step's working set (~250 MB) is larger than L2.
-    host = [t.cpu().pin_memory() for t in (q, k, v, do)]
-    outs = [[torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
-            for _ in range(2)]
+    # The pinned buffers are allocated (first touched) from the GPU's NUMA-local cores, so
+    # the copies do not cross the socket interconnect.
+    saved_cpus = os.sched_getaffinity(0)
+    local_cpus = gpu_local_cpus(local)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
+    try:
+        host = [t.cpu().pin_memory() for t in (q, k, v, do)]
+        outs = [[torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+                for _ in range(2)]
+    finally:
+        os.sched_setaffinity(0, saved_cpus)
     dbuf = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+
+    def link_gbps(dst, src, reps: int = 3) -> float:
+        """Bandwidth of one plain pinned copy of a 25 MB tensor (median of reps)."""
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            dst.copy_(src, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(b))
+        return src.numel() * src.element_size() / statistics.median(times) / 1e6
+
+    link = {"h2d": round(link_gbps(dbuf[0][0], host[0]), 1),
+            "d2h": round(link_gbps(outs[0][0], dbuf[0][0]), 1)}
     for bset in dbuf:
         for t in bset[:3]:
             t.requires_grad_(True)
@@ -461,7 +502,10 @@ def run_ours(args) -> None:
                     "h2d_bytes_per_step": 4 * tensor_bytes, "d2h_bytes_per_step": 3 * tensor_bytes,
                     "ms_per_step": round(e2e_ms / args.steps, 4),
                     "timing": "one region over all steps; copies in/out on their own streams "
-                              "overlap the neighbouring steps' compute (double-buffered inputs)"},
+                              "overlap the neighbouring steps' compute (double-buffered inputs)",
+                    "link_GBps": link,
+                    "pinned_on": (f"{len(local_cpus)} GPU-local cores" if local_cpus
+                                  else "any core (NVML gave no affinity)")},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
