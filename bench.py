@@ -324,6 +324,59 @@ def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """The cached-sampling K/V path (SURVEY next row 1) at the generation config (B=64,
+    H=12, head_dim 64, 16-token blocks, max_seq_len 1024): one layer of one denoising step of
+    the last block (1008 cached tokens), through bd3_qkv_rope_cache (q out, k/v written in
+    place) beside the reference's ops for the same step (model/modules.py:395-417: rearrange,
+    RoPE on q and k, torch.cat of cache and new K/V, run here with torch on the GPU); and a
+    1024-token prefill of all 64 sequences through the kernel, against the HBM roofline."""
+    from bd3attn import ops
+    B, Hh, Dd, S, L, max_pos = 64, H, D, 16, 1008, 1024
+    pos = torch.arange(max_pos, dtype=torch.float64)
+    inv = 10000.0 ** (-torch.arange(0, Dd, 2, dtype=torch.float64) / Dd)
+    ang = pos[:, None] * inv[None, :]  # the reference's RoPE tables (model/modules.py:196-207)
+    sin, cos = torch.sin(ang).float().to(dev), torch.cos(ang).float().to(dev)
+    g = torch.Generator().manual_seed(8)
+    qkv = torch.randn(B, S, 3 * Hh * Dd, generator=g).bfloat16().to(dev)
+    kc = torch.zeros(B, Hh, max_pos, Dd, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros_like(kc)
+    q_out = torch.empty(B, Hh, S, Dd, dtype=torch.bfloat16, device=dev)
+    ours = statistics.median(time_steps(
+        lambda: ops.qkv_rope_cache_raw(qkv, Hh, cos, sin, kc, vc, L, pos0=L, q_out=q_out),
+        reps, l2))
+    k_hist, v_hist = kc[:, :, :L].contiguous(), vc[:, :, :L].contiguous()
+    positions = torch.arange(L, L + S, device=dev)
+
+    def rope(x):
+        s_, c_ = sin[positions].to(x.dtype), cos[positions].to(x.dtype)
+        x1, x2 = x.chunk(2, dim=-1)
+        return torch.cat([x1 * c_ - x2 * s_, x1 * s_ + x2 * c_], dim=-1)
+
+    def ref_step():
+        q, k, v = qkv.view(B, S, 3, Hh, Dd).permute(2, 0, 3, 1, 4)
+        rope(q)
+        torch.cat([k_hist, rope(k)], dim=-2)
+        torch.cat([v_hist, v], dim=-2)
+    for _ in range(3):
+        ref_step()
+    ref = statistics.median(time_steps(ref_step, reps, l2))
+    step_bytes = 2 * B * S * 3 * Hh * Dd * 2  # read the projection, write q, k, v
+    out = {"decode_step_layer_b64": {"us": round(ours * 1e3, 2), "bytes": step_bytes,
+                                     "reference_ops_us": round(ref * 1e3, 2)}}
+    S2 = 1024
+    qkv2 = torch.randn(B, S2, 3 * Hh * Dd, generator=g).bfloat16().to(dev)
+    q2 = torch.empty(B, Hh, S2, Dd, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ops.qkv_rope_cache_raw(qkv2, Hh, cos, sin, kc, vc, 0, pos0=0, q_out=q2)
+    t = statistics.median(time_steps(
+        lambda: ops.qkv_rope_cache_raw(qkv2, Hh, cos, sin, kc, vc, 0, pos0=0, q_out=q2), reps, l2))
+    by = 2 * B * S2 * 3 * Hh * Dd * 2
+    out["prefill_b64_s1024"] = {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
+                                "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
+    return out
+
+
 def run_ours(args) -> None:
     world, rank, local = dist_setup(args.gpus)
     from bd3attn import ops
@@ -476,6 +529,7 @@ def run_ours(args) -> None:
                                                          * 1e-3) / 1e12, 2)}
     if not args.no_decode:
         extra["decode"] = decode_extras(ops, dev, l2, peaks)
+        extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {

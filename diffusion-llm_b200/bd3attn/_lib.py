@@ -42,6 +42,8 @@ SIGNATURES = {
                                       _sz, _vp]),
     "bd3_lse_merge": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                              _i64, _pi64, _i32, _vp]),
+    "bd3_qkv_rope_cache": (_i32, [_vp, _pi64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64,
+                                  _vp, _vp, _vp, _pi64, _i64, _i64, _i32, _vp]),
     "bd3_profile_enable": (_i32, [_i32]),
     "bd3_profile_collect": (_i32, [ctypes.POINTER(ctypes.c_double), _pi32]),
     "bd3_debug_ranges": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi32]),

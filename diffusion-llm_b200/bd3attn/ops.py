@@ -168,7 +168,8 @@ def lse_merge_raw(parts, lses, out_dtype=torch.bfloat16):
 
 
 def device_status(clear: bool = True) -> int:
-    """Sticky device-side error bits (1: a bounded wait ran out). Synchronises."""
+    """Sticky device-side error bits (1: a bounded wait ran out; 2: a kernel rejected its
+    launch; 4: a RoPE position was outside the table). Synchronises."""
     return int(LIB.bd3_device_status(1 if clear else 0))
 
 
@@ -210,9 +211,52 @@ def _(q, k, v, block_size):
     return q.new_empty(tuple(q.shape))
 
 
+def qkv_rope_cache_raw(qkv, n_heads: int, cos_table, sin_table, k_cache, v_cache, row0: int,
+                       positions=None, pos0: int = 0, q_out=None):
+    """Split a fused QKV projection, rotate q and k (the reference's RoPE), write k and v to
+    rows [row0, row0 + seq) of the caches in place and q to q_out; returns q_out.
+
+    qkv: (B, S, 3 * n_heads * D) with its last dim ordered (three, heads, head_dim);
+    cos_table, sin_table: (max_pos, D / 2) fp32 (RoPE's buffers); k_cache, v_cache:
+    (B, n_heads, rows, D) in qkv's dtype; positions: (S,) int64 absolute positions on the
+    device, or None for pos0, pos0 + 1, ...; q_out: (B, n_heads, S, D) or None to allocate.
+    """
+    _check_cuda(qkv, cos_table, sin_table, k_cache, v_cache)
+    if qkv.dim() != 3:
+        raise AssertionError("qkv must be (batch, seq, 3 * n_heads * head_dim)")
+    B, S, F = qkv.shape
+    if F % (3 * n_heads):
+        raise AssertionError("qkv's last dim must be 3 * n_heads * head_dim")
+    D = F // (3 * n_heads)
+    if qkv.stride(-1) != 1:
+        qkv = qkv.contiguous()
+    if q_out is None:
+        q_out = torch.empty((B, n_heads, S, D), dtype=qkv.dtype, device=qkv.device)
+    for name, t in (("k_cache", k_cache), ("v_cache", v_cache), ("q_out", q_out)):
+        if t.dtype != qkv.dtype or t.stride(-1) != 1 or t.shape[0] != B or t.shape[1] != n_heads \
+                or t.shape[-1] != D:
+            raise AssertionError(f"{name} must be (B, n_heads, rows, head_dim) in qkv's dtype")
+    if k_cache.shape[2] != v_cache.shape[2]:
+        raise AssertionError("k_cache and v_cache must have the same rows")
+    cos_table = cos_table.float().contiguous()
+    sin_table = sin_table.float().contiguous()
+    if positions is not None:
+        positions = positions.to(device=qkv.device, dtype=torch.int64).contiguous()
+        if positions.numel() != S:
+            raise AssertionError("positions must have one entry per token")
+    strides = i64_array(_s3(q_out) + _s3(k_cache) + _s3(v_cache))
+    with torch.cuda.device(qkv.device):
+        check("bd3_qkv_rope_cache", LIB.bd3_qkv_rope_cache(
+            _ptr(qkv), i64_array((qkv.stride(0), qkv.stride(1))), B, S, n_heads, D,
+            _ptr(positions), int(pos0), _ptr(cos_table), _ptr(sin_table), cos_table.shape[0],
+            _ptr(q_out), _ptr(k_cache), _ptr(v_cache), strides, int(row0), k_cache.shape[2],
+            _code(qkv.dtype), _stream(qkv)))
+    return q_out
+
+
 # ---------------------------------------------------------------------------------------
 PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_prep", "bwd_dq_convert", "bwd_fused",
-                   "decode", "decode_combine")
+                   "decode", "decode_combine", "qkv_rope_cache")
 
 
 def profile_enable(on: bool = True) -> None:

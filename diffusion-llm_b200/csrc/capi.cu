@@ -13,6 +13,7 @@
 #include "attn_bwd.cuh"
 #include "attn_fwd.cuh"
 #include "decode.cuh"
+#include "kv_rope.cuh"
 
 namespace {
 
@@ -125,7 +126,7 @@ int set_smem(K kernel, uint32_t bytes, int slot) {
 
 
 // ---- optional per-kernel timing (bd3_profile_*): CUDA event pairs around each launch ----
-enum ProfId { kPfFwd = 0, kPfPrefill, kPfDelta, kPfDq, kPfDkdv, kPfDecode, kPfCombine, kPfNum };
+enum ProfId { kPfFwd = 0, kPfPrefill, kPfDelta, kPfDq, kPfDkdv, kPfDecode, kPfCombine, kPfRope, kPfNum };
 constexpr int kProfCap = 8192;
 struct Prof {
   bool on = false;
@@ -712,6 +713,75 @@ int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out
   return check_launch("decode_combine_kernel launch");
 }
 
+int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, int64_t S,
+                       int64_t H, int64_t D, const int64_t* positions, int64_t pos0,
+                       const float* cos_table, const float* sin_table, int64_t max_pos,
+                       void* q_out, void* k_cache, void* v_cache, const int64_t* strides,
+                       int64_t cache_row0, int64_t cache_rows, int dtype, void* stream) {
+  if (dtype < BD3_BF16 || dtype > BD3_F32) return fail(BD3_ERR_INVALID, "bad dtype %d", dtype);
+  if (B < 1 || S < 1 || H < 1 || D < 1) return fail(BD3_ERR_INVALID, "sizes must be >= 1");
+  if (D % 16 != 0 || D > 1024)
+    return fail(BD3_ERR_UNSUPPORTED, "head_dim must be a multiple of 16 up to 1024 (got %lld)",
+                (long long)D);
+  if (qkv == nullptr || cos_table == nullptr || sin_table == nullptr || k_cache == nullptr ||
+      v_cache == nullptr)
+    return fail(BD3_ERR_INVALID, "qkv, the RoPE tables and both caches are required");
+  if (max_pos < 1) return fail(BD3_ERR_INVALID, "max_pos must be >= 1");
+  if (positions == nullptr && (pos0 < 0 || pos0 + S > max_pos))
+    return fail(BD3_ERR_INVALID, "positions [%lld, %lld) outside the RoPE table of %lld rows",
+                (long long)pos0, (long long)(pos0 + S), (long long)max_pos);
+  if (cache_row0 < 0 || cache_row0 + S > cache_rows)
+    return fail(BD3_ERR_INVALID, "cache rows [%lld, %lld) outside a cache of %lld rows",
+                (long long)cache_row0, (long long)(cache_row0 + S), (long long)cache_rows);
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  const int64_t eb = static_cast<int64_t>(elem_bytes(dtype));
+  auto aligned = [&](const void* ptr, const int64_t* st, int n) {
+    if (reinterpret_cast<uintptr_t>(ptr) % 16) return false;
+    for (int i = 0; i < n; ++i)
+      if ((st[i] * eb) % 16) return false;
+    return true;
+  };
+  if (!aligned(qkv, qkv_strides, 2)) return fail(BD3_ERR_INVALID, "qkv: pointer and strides must be 16-byte aligned");
+  if (q_out != nullptr && !aligned(q_out, strides, 3))
+    return fail(BD3_ERR_INVALID, "q_out: pointer and strides must be 16-byte aligned");
+  if (!aligned(k_cache, strides + 3, 3) || !aligned(v_cache, strides + 6, 3))
+    return fail(BD3_ERR_INVALID, "k_cache/v_cache: pointer and strides must be 16-byte aligned");
+  if (reinterpret_cast<uintptr_t>(cos_table) % 16 || reinterpret_cast<uintptr_t>(sin_table) % 16)
+    return fail(BD3_ERR_INVALID, "RoPE tables must be 16-byte aligned");
+  const int64_t threads = B * S * H * (D / 16);
+  if ((threads + 255) / 256 > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "too many tokens");
+  bd3::RopeCacheParams p{};
+  p.qkv = qkv;
+  p.qkv_sb = qkv_strides[0];
+  p.qkv_ss = qkv_strides[1];
+  p.positions = reinterpret_cast<const long long*>(positions);
+  p.pos0 = pos0;
+  p.cos_table = cos_table;
+  p.sin_table = sin_table;
+  p.max_pos = max_pos;
+  p.q_out = q_out;
+  if (q_out != nullptr) {
+    p.q_sb = strides[0]; p.q_sh = strides[1]; p.q_ss = strides[2];
+  }
+  p.k_cache = k_cache;
+  p.k_sb = strides[3]; p.k_sh = strides[4]; p.k_ss = strides[5];
+  p.v_cache = v_cache;
+  p.v_sb = strides[6]; p.v_sh = strides[7]; p.v_ss = strides[8];
+  p.row0 = cache_row0;
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.H = static_cast<int>(H);
+  p.D = static_cast<int>(D);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  {
+    ProfScope ps(kPfRope, st);
+    if (dtype == BD3_BF16) bd3::qkv_rope_cache_kernel<0><<<blocks, 256, 0, st>>>(p);
+    else if (dtype == BD3_F16) bd3::qkv_rope_cache_kernel<1><<<blocks, 256, 0, st>>>(p);
+    else bd3::qkv_rope_cache_kernel<2><<<blocks, 256, 0, st>>>(p);
+  }
+  return check_launch("qkv_rope_cache_kernel launch");
+}
 
 int bd3_profile_enable(int on) {
   Prof& p = prof();

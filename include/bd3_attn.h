@@ -43,7 +43,8 @@ BD3_API int bd3_version(void);
 /* Message of the last failed call on this host thread ("" if none). */
 BD3_API const char* bd3_last_error(void);
 /* Sticky device-side status bits of the current device (1: a bounded wait inside a kernel
- * ran out; 2: a kernel rejected its launch parameters). Synchronises the device. Clears the
+ * ran out; 2: a kernel rejected its launch parameters; 4: a RoPE position was outside the
+ * table). Synchronises the device. Clears the
  * bits when `clear` is non-zero. Returns a negative value if the CUDA call itself failed. */
 BD3_API int bd3_device_status(int clear);
 
@@ -143,13 +144,35 @@ BD3_API int bd3_lse_merge(const float* parts, const float* lses, void* o, float*
                   int64_t part_bh, int64_t lse_g, int64_t lse_bh, const int64_t* o_strides,
                   int out_dtype, void* stream);
 
+/* Fused QKV split + rotary embedding + in-place KV-cache write for one attention layer.
+ * Replaces model/modules.py:395-417 (the rearrange of the fused projection, self.rope on q
+ * and k, and the torch.cat of the cached and the new K/V) and KVCache.append
+ * (model/kv_cache.py:42-55): k and v go straight into rows [cache_row0, cache_row0 + S) of
+ * preallocated cache tensors, so no step or commit copies the cache. RoPE is the reference's
+ * rotate-half form with its own tables; results are bit-identical to the reference's ops.
+ *   qkv: (B, S, 3*H*D) projection output whose last dim is ordered (three, heads, head_dim)
+ *        and contiguous; qkv_strides[2] = (batch, seq) in elements.
+ *   positions: device int64 (S,) absolute positions, or NULL for pos0 + s.
+ *   cos_table, sin_table: device fp32 (max_pos, D/2) row-major (RoPE.cos_table/sin_table).
+ *   q_out: (B, H, S, D) rotated queries, or NULL. k_cache, v_cache: (B, H, cache_rows, D).
+ *   strides[9] = q_out, k_cache, v_cache (batch, head, seq) in elements.
+ * dtype: BD3_BF16, BD3_F16 or BD3_F32 (all tensors but the tables). head_dim % 16 == 0;
+ * pointers and strides 16-byte aligned. A device position outside [0, max_pos) (the
+ * reference raises IndexError) leaves its token unwritten and sets device status bit 4. */
+BD3_API int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, int64_t S,
+                               int64_t H, int64_t D, const int64_t* positions, int64_t pos0,
+                               const float* cos_table, const float* sin_table, int64_t max_pos,
+                               void* q_out, void* k_cache, void* v_cache, const int64_t* strides,
+                               int64_t cache_row0, int64_t cache_rows, int dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Per-kernel timing for benchmarks. While enabled, every launch is bracketed by a pair of
  * CUDA events on its own stream (at most 8192 launches are kept). bd3_profile_collect()
  * waits for them and writes, per kernel id (0 training forward, 1 prefill forward, 2 backward
- * prep, 3 dQ convert, 4 fused backward, 5 decode, 6 decode combine), the summed milliseconds
+ * prep, 3 dQ convert, 4 fused backward, 5 decode, 6 decode combine, 7 QKV RoPE cache write),
+ * the summed milliseconds
  * and launch counts to
- * total_ms[7] and counts[7]; it returns 7 and forgets the recorded launches.
+ * total_ms[8] and counts[8]; it returns 8 and forgets the recorded launches.
  */
 BD3_API int bd3_profile_enable(int on);
 BD3_API int bd3_profile_collect(double* total_ms, int32_t* counts);

@@ -6,7 +6,9 @@ Run once, in a checkout where the reference (tusharsonthalia/diffusion-llm) is i
 
 It imports the reference's own ``model/bd3lm.py:block_diff_mask`` (:10-52) and
 ``model/modules.py:scaled_dot_product_attention`` (:738-771), runs them on seeded
-inputs on the CPU, and writes ``tests/golden/golden.npz``. Inputs are bf16-valued (the
+inputs on the CPU, and writes ``tests/golden/golden.npz``; ``kv_cases`` does the same for
+``model/modules.py:RoPE`` (:164-240) and ``model/kv_cache.py:KVCache`` (:9-55) into
+``tests/golden/golden_kv.npz``. Inputs are bf16-valued (the
 dtype of the CUDA path) and stored as raw bf16 bits; reference outputs are stored in fp32,
 exactly as the reference returns them for fp32 inputs. The tests read only the .npz; the
 reference is not needed to run them.
@@ -103,6 +105,48 @@ def main(ref_root: str) -> None:
     out[f"{tag}_o"] = o.numpy().astype(np.float32)
 
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden.npz")
+    np.savez_compressed(path, **out)
+    print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
+    kv_cases(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_kv.npz"))
+
+
+# (dtype, seq, positions) for the reference's RoPE on (1, 2, seq, 64) activations
+ROPE_CASES = [("bf16", 5, [0, 3, 7, 20, 63]), ("f16", 4, [1, 2, 3, 4]),
+              ("f32", 6, [63, 0, 31, 32, 5, 6])]
+_TORCH_DT = {"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}
+
+
+def kv_cases(path: str) -> None:
+    """RoPE (model/modules.py:164-240) and KVCache (model/kv_cache.py:9-55) fixtures: the
+    reference's own tables, rotated activations and concatenated cache contents."""
+    from model import modules  # noqa: E402
+    from model.kv_cache import KVCache  # noqa: E402
+
+    out = {}
+    rope = modules.RoPE(64, 64)
+    out["rope_sin"] = rope.sin_table.numpy()
+    out["rope_cos"] = rope.cos_table.numpy()
+    gen = torch.Generator().manual_seed(99)
+    for dt, seq, pos in ROPE_CASES:
+        x = (3 * torch.randn((1, 2, seq, 64), generator=gen)).to(_TORCH_DT[dt])
+        y = rope(x, torch.tensor(pos))
+        out[f"rope_{dt}_x"] = x.float().numpy()
+        out[f"rope_{dt}_pos"] = np.array(pos, dtype=np.int64)
+        out[f"rope_{dt}_y"] = y.float().numpy()
+    # two layers, three appends of 2, 3 and 1 tokens
+    cache = KVCache.empty(2)
+    for i, s in enumerate((2, 3, 1)):
+        for layer in range(2):
+            k = torch.randn((1, 2, s, 64), generator=gen)
+            v = torch.randn((1, 2, s, 64), generator=gen)
+            out[f"kv_append{i}_l{layer}_k"] = k.numpy()
+            out[f"kv_append{i}_l{layer}_v"] = v.numpy()
+            cache.append(layer, k, v)
+    for layer in range(2):
+        k, v = cache.get(layer)
+        out[f"kv_final_l{layer}_k"] = k.numpy()
+        out[f"kv_final_l{layer}_v"] = v.numpy()
+    out["kv_length"] = np.array(cache.length, dtype=np.int64)
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
 
