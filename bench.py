@@ -377,6 +377,46 @@ def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """One denoising step of the block sampler (SURVEY next row 2) at the generation config:
+    B=64 sequences, a 16-token block, vocabulary 50258, bf16 logits (the backbone runs under
+    autocast), every token still masked (a block's first step). bd3_subs_sample beside the
+    reference's ops for the same step (model/subs.py:11-43, sample/sampler.py:11-34, 100-122:
+    SUBS, exp, double, weights, Gumbel-max in float64, where), run with torch on the GPU.
+    Algorithmic bytes: the logits once."""
+    from bd3attn.sampler import subs_sample_step
+    B, S, V = 64, 16, 50258
+    mask = V - 1
+    g = torch.Generator().manual_seed(9)
+    logits = (3 * torch.randn(B, S, V, generator=g)).bfloat16().to(dev)
+    block = torch.full((B, S), mask, dtype=torch.int64, device=dev)
+    t, s_ = 1.0, 0.9375
+    out = torch.empty_like(block)
+    ours = statistics.median(time_steps(
+        lambda: subs_sample_step(logits, block, mask, t, s_, out=out), reps, l2))
+
+    def ref_step():
+        bias = torch.zeros(V, device=dev, dtype=logits.dtype)
+        bias[mask] = -1e6
+        x = logits + bias
+        shifted = x - x.amax(dim=-1, keepdim=True)
+        lp = shifted - torch.log(torch.exp(shifted).sum(dim=-1, keepdim=True))
+        carry = torch.full_like(lp, -1e6).scatter(-1, block.unsqueeze(-1), 0.0)
+        lp = torch.where((block != mask).unsqueeze(-1), carry, lp)
+        q = torch.exp(lp).double() * (1 - s_ / t)
+        q[..., mask] = s_ / t
+        u = torch.rand_like(q, dtype=torch.float64)
+        new = torch.argmax(q / (1e-10 - torch.log(u + 1e-10)), dim=-1)
+        return torch.where(block != mask, block, new)
+    for _ in range(3):
+        ref_step()
+    ref = statistics.median(time_steps(ref_step, reps, l2))
+    by = B * S * V * 2
+    return {"step_b64_v50258_bf16": {"us": round(ours * 1e3, 2), "reference_ops_us": round(ref * 1e3, 2),
+                                     "GBps": round(by / ours / 1e6, 1),
+                                     "frac_hbm": round(by / ours / 1e6 / peaks["hbm_gbs"], 4)}}
+
+
 def run_ours(args) -> None:
     world, rank, local = dist_setup(args.gpus)
     from bd3attn import ops
@@ -530,6 +570,7 @@ def run_ours(args) -> None:
     if not args.no_decode:
         extra["decode"] = decode_extras(ops, dev, l2, peaks)
         extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
+        extra["sampler"] = sampler_extras(dev, l2, peaks)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {

@@ -256,7 +256,7 @@ def qkv_rope_cache_raw(qkv, n_heads: int, cos_table, sin_table, k_cache, v_cache
 
 # ---------------------------------------------------------------------------------------
 PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_prep", "bwd_dq_convert", "bwd_fused",
-                   "decode", "decode_combine", "qkv_rope_cache")
+                   "decode", "decode_combine", "qkv_rope_cache", "subs_sample")
 
 
 def profile_enable(on: bool = True) -> None:
@@ -267,8 +267,8 @@ def profile_enable(on: bool = True) -> None:
 
 def profile_collect() -> dict:
     """{kernel name: (total ms, launches)} for the launches since the last collect."""
-    ms = (ctypes.c_double * 8)()
-    cnt = (ctypes.c_int32 * 8)()
+    ms = (ctypes.c_double * 16)()
+    cnt = (ctypes.c_int32 * 16)()
     n = LIB.bd3_profile_collect(ms, cnt)
     if n < 0:
         check("bd3_profile_collect", -n)

@@ -14,6 +14,7 @@
 #include "attn_fwd.cuh"
 #include "decode.cuh"
 #include "kv_rope.cuh"
+#include "sampler.cuh"
 
 namespace {
 
@@ -126,7 +127,10 @@ int set_smem(K kernel, uint32_t bytes, int slot) {
 
 
 // ---- optional per-kernel timing (bd3_profile_*): CUDA event pairs around each launch ----
-enum ProfId { kPfFwd = 0, kPfPrefill, kPfDelta, kPfDq, kPfDkdv, kPfDecode, kPfCombine, kPfRope, kPfNum };
+enum ProfId {
+  kPfFwd = 0, kPfPrefill, kPfDelta, kPfDq, kPfDkdv, kPfDecode, kPfCombine, kPfRope, kPfSample,
+  kPfNum
+};
 constexpr int kProfCap = 8192;
 struct Prof {
   bool on = false;
@@ -781,6 +785,47 @@ int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, i
     else bd3::qkv_rope_cache_kernel<2><<<blocks, 256, 0, st>>>(p);
   }
   return check_launch("qkv_rope_cache_kernel launch");
+}
+
+int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B, int64_t S,
+                    int64_t V, const int64_t* xt, int64_t mask_index, double t, double s,
+                    uint64_t seed, uint64_t offset, const double* uniforms, int64_t* out,
+                    int dtype, void* stream) {
+  if (dtype != BD3_BF16 && dtype != BD3_F32)  // the reference's SUBS cannot hold -1e6 in fp16
+    return fail(BD3_ERR_INVALID, "logits must be bf16 or fp32 (got dtype %d)", dtype);
+  if (B < 1 || S < 1 || V < 2) return fail(BD3_ERR_INVALID, "need B, S >= 1 and V >= 2");
+  if (V > 2147483647LL / 2 || B * S > 2147483647LL)
+    return fail(BD3_ERR_UNSUPPORTED, "vocabulary or batch too large");
+  if (mask_index < 0 || mask_index >= V)
+    return fail(BD3_ERR_INVALID, "mask_index %lld outside the vocabulary of %lld",
+                (long long)mask_index, (long long)V);
+  if (logits == nullptr || xt == nullptr || out == nullptr)
+    return fail(BD3_ERR_INVALID, "logits, xt and out are required");
+  if (!(t > 0.0)) return fail(BD3_ERR_INVALID, "t must be > 0 (the step divides by it)");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  bd3::SampleParams p{};
+  p.logits = logits;
+  p.l_sb = logit_strides[0];
+  p.l_ss = logit_strides[1];
+  p.xt = reinterpret_cast<const long long*>(xt);
+  p.out = reinterpret_cast<long long*>(out);
+  p.u = uniforms;
+  p.seed = seed;
+  p.offset = offset;
+  p.keep = 1.0 - s / t;  // the reference's Python floats: (1 - s / t) and s / t
+  p.stay = s / t;
+  p.mask_index = mask_index;
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.V = static_cast<int>(V);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned blocks = static_cast<unsigned>(B * S);
+  {
+    ProfScope ps(kPfSample, st);
+    if (dtype == BD3_BF16) bd3::subs_sample_kernel<0><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    else bd3::subs_sample_kernel<2><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+  }
+  return check_launch("subs_sample_kernel launch");
 }
 
 int bd3_profile_enable(int on) {

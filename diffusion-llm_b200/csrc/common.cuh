@@ -325,6 +325,15 @@ __device__ __forceinline__ float2 exp2_fma2(float2 t) {
                      __int_as_float(__float_as_int(p.y) + (__float_as_int(y.y) << 23)));
 }
 
+// Round a float through dtype kDtype (0 bf16, 1 fp16, 2 fp32: identity) and back, as a
+// PyTorch elementwise op on tensors of that dtype rounds its fp32 result.
+template <int kDtype>
+__device__ __forceinline__ float rnd(float x) {
+  if constexpr (kDtype == 0) return __bfloat162float(__float2bfloat16_rn(x));
+  else if constexpr (kDtype == 1) return __half2float(__float2half_rn(x));
+  else return x;
+}
+
 template <bool kBF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (kBF16) {

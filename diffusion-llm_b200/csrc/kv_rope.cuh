@@ -45,14 +45,6 @@ struct RopeCacheParams {
   int B, S, H, D;
 };
 
-// Round through the activation dtype (the reference's .to(x.dtype) and its elementwise ops).
-template <int kDtype>
-__device__ __forceinline__ float rnd(float x) {
-  if constexpr (kDtype == 0) return __bfloat162float(__float2bfloat16_rn(x));
-  else if constexpr (kDtype == 1) return __half2float(__float2half_rn(x));
-  else return x;
-}
-
 // kN consecutive elements moved as 16-byte pieces (8 two-byte values or 4 floats per piece;
 // the host checks that every tensor's base and strides are 16-byte aligned, and element
 // offsets here are multiples of 8).

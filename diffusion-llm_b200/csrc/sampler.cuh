@@ -1,0 +1,268 @@
+// One ancestral denoising step of the BD3-LM sampler for a block of tokens (sm_100a).
+//
+// Replaces, per step, the reference's
+//   log_probs = subs_parameterization(logits, block, mask_index)      model/subs.py:11-43
+//   q = torch.exp(log_probs).double() * (1 - s / t); q[..., mask] = s / t
+//   new = sample_categorical(q)                                       sample/sampler.py:11-34
+//   block = torch.where(block != mask_index, block, new)              sample/sampler.py:114-122
+// with one kernel that reads each masked row's logits and writes one token. Rows whose token
+// is already unmasked keep it (the reference computes them and discards the result). For a
+// masked row (one CTA, V logits):
+//   lp_j   = log_softmax(logits + bias)_j, bias = -1e6 at mask_index: shifted = x - max,
+//            sum of exp(shifted), shifted - log(sum) (model/modules.py:791-799), each op
+//            rounded to the logits' dtype as the reference's tensors of that dtype are (the
+//            sum accumulates in fp32 and is rounded once, as torch.sum does)
+//   q_j    = (double) exp(lp_j) * (1 - s/t) for j != mask_index;  q_mask = s/t
+// The draw is either a replay of the reference's own: u_j read from a caller's float64
+// tensor (the reference's torch.rand_like), g_j = EPS - log(u_j + EPS), token = argmax_j
+// q_j / g_j (the first index among equal maxima, as torch.argmax); or, in production, an
+// exact draw from the same distribution q / sum(q) by inverse CDF with one uniform per row:
+// the elements are ordered (thread t, then j = t, t + T, t + 2T, ...), each thread sums its
+// q_j in float64 in that order, a block scan (Hillis-Steele within warps, then over the
+// warp totals) gives every thread its slice [excl, incl) of [0, total), and
+// r * total with r = (x << 21 | y >> 11) * 2^-53 from words x, y of Philox4x32-10 (Salmon,
+// Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011) at counter
+// (row, offset lo, offset hi, 0x5A3) under key = seed falls in one slice, whose thread walks
+// it (the smallest claimed index wins where rounding makes slices overlap; a walk that
+// rounds past its slice takes its last nonzero element). float64 sums keep tokens with
+// probability down to ~1e-16 of the row's mass, as the reference's float64 noise does.
+#pragma once
+
+#include "common.cuh"
+
+namespace bd3 {
+
+constexpr int kSampleThreads = 512;
+
+struct SampleParams {
+  const void* logits;        // (B, S, V), vocab contiguous
+  long long l_sb, l_ss;
+  const long long* xt;       // (B, S) current tokens
+  long long* out;            // (B, S) next tokens (may alias xt)
+  const double* u;           // (B, S, V) contiguous uniforms, or null for Philox
+  unsigned long long seed, offset;
+  double keep;               // 1 - s/t, the weight of the unmasking tokens
+  double stay;               // s/t, the weight of staying masked
+  long long mask_index;
+  int B, S, V;
+};
+
+// ---- Philox4x32-10 (the published round function and Weyl key schedule) ----------------
+struct U4 {
+  uint32_t x, y, z, w;
+};
+__device__ __forceinline__ U4 philox4x32_10(U4 c, uint32_t k0, uint32_t k1) {
+  constexpr uint32_t kM0 = 0xD2511F53u, kM1 = 0xCD9E8D57u;
+  constexpr uint32_t kW0 = 0x9E3779B9u, kW1 = 0xBB67AE85u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(kM0, c.x), lo0 = kM0 * c.x;
+    const uint32_t hi1 = __umulhi(kM1, c.z), lo1 = kM1 * c.z;
+    c = U4{hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0};
+    k0 += kW0;
+    k1 += kW1;
+  }
+  return c;
+}
+__device__ __forceinline__ double u53(uint32_t hi, uint32_t lo) {
+  const unsigned long long m = (static_cast<unsigned long long>(hi) << 21) | (lo >> 11);
+  return static_cast<double>(m) * 0x1.0p-53;
+}
+
+template <int kDtype>
+__device__ __forceinline__ float logit_at(const void* row, int j) {
+  if constexpr (kDtype == 0) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(row)[j]);
+  else if constexpr (kDtype == 1) return __half2float(reinterpret_cast<const __half*>(row)[j]);
+  else return reinterpret_cast<const float*>(row)[j];
+}
+
+// Block-wide reductions over kSampleThreads threads through shared memory.
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < kSampleThreads / 32 ? red[l] : -INFINITY;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return __shfl_sync(0xffffffffu, v, 0);  // lanes 0-15 hold the result; give it to all
+}
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < kSampleThreads / 32 ? red[l] : 0.f;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return __shfl_sync(0xffffffffu, v, 0);
+}
+
+// (score, index) with the larger score, the smaller index on a tie (torch.argmax's first max).
+__device__ __forceinline__ void best_of(double& s, int& i, double s2, int i2) {
+  if (s2 > s || (s2 == s && i2 < i)) s = s2, i = i2;
+}
+
+template <int kDtype>
+__global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const SampleParams p) {
+  __shared__ float red[kSampleThreads / 32];
+  __shared__ double rs[kSampleThreads / 32];
+  __shared__ double wscan[kSampleThreads / 32];
+  __shared__ double last_incl[kSampleThreads / 32];
+  __shared__ int ri[kSampleThreads / 32];
+  const int row = blockIdx.x;
+  const int b = row / p.S, i = row % p.S;
+  const long long tok = p.xt[static_cast<long long>(b) * p.S + i];
+  if (tok != p.mask_index) {  // carry-over: the reference's where() keeps the token
+    if (threadIdx.x == 0) p.out[static_cast<long long>(b) * p.S + i] = tok;
+    return;
+  }
+  const void* lrow = reinterpret_cast<const uint8_t*>(p.logits) +
+                     (b * p.l_sb + i * p.l_ss) * (kDtype == 2 ? 4 : 2);
+  const int mask = static_cast<int>(p.mask_index);
+  const float bias = rnd<kDtype>(-1e6f);  // model/subs.py:8
+  // pass 1: max and sum of exp(x - max) of the biased logits; kUnroll independent loads in
+  // flight per thread
+  constexpr int kUnroll = 8;
+  auto biased = [&](int j) {
+    const float x = logit_at<kDtype>(lrow, j);
+    return j == mask ? rnd<kDtype>(x + bias) : x;
+  };
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
+    float x[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int jj = j + k * kSampleThreads;
+      x[k] = jj < p.V ? biased(jj) : -INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) mx = fmaxf(mx, x[k]);
+  }
+  mx = block_max(mx, red);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
+    float x[kUnroll];
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const int jj = j + k * kSampleThreads;
+      x[k] = jj < p.V ? biased(jj) : -INFINITY;
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+      if (j + k * kSampleThreads < p.V) sum += rnd<kDtype>(expf(rnd<kDtype>(x[k] - mx)));
+  }
+  sum = rnd<kDtype>(block_sum(sum, red));
+  const float lse = rnd<kDtype>(logf(sum));
+  // pass 2: q_j in float64 (the reference's exp(log_probs).double() * (1 - s/t), s/t at
+  // mask_index), then one draw.
+  auto q64 = [&](int j) -> double {
+    if (j == mask) return p.stay;
+    const float lp = rnd<kDtype>(rnd<kDtype>(logit_at<kDtype>(lrow, j) - mx) - lse);
+    return static_cast<double>(rnd<kDtype>(expf(lp))) * p.keep;
+  };
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  long long pick;
+  if (p.u != nullptr) {
+    // replay of the reference's own draw: argmax_j q_j / (EPS - log(u_j + EPS)) in float64
+    const double* urow = p.u + static_cast<long long>(row) * p.V;
+    double best = -1.0;
+    int best_i = 0x7fffffff;
+    for (int j = threadIdx.x; j < p.V; j += kSampleThreads)
+      best_of(best, best_i, q64(j) / (1e-10 - log(urow[j] + 1e-10)), j);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const double s2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, best_i, o);
+      best_of(best, best_i, s2, i2);
+    }
+    if (l == 0) rs[w] = best, ri[w] = best_i;
+    __syncthreads();
+    best = l < kSampleThreads / 32 ? rs[l] : -1.0;
+    best_i = l < kSampleThreads / 32 ? ri[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+      const double s2 = __shfl_xor_sync(0xffffffffu, best, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, best_i, o);
+      best_of(best, best_i, s2, i2);
+    }
+    pick = best_i;
+  } else {
+    // inverse CDF over the element order (thread t, then j = t, t + T, t + 2T, ...): each
+    // thread sums its q_j in that order, a block scan gives each thread its slice
+    // [excl_t, incl_t) of [0, total), and one Philox uniform r per row selects r * total.
+    double part = 0.0;
+    for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
+      double q[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) {
+        const int jj = j + k * kSampleThreads;
+        q[k] = jj < p.V ? q64(jj) : 0.0;
+      }
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k) part += q[k];
+    }
+    // inclusive scan: within warps (Hillis-Steele), then of the warp totals in warp 0
+    double x = part;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, x, o);
+      if (l >= o) x += y;
+    }
+    if (l == 31) rs[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      double v = l < kSampleThreads / 32 ? rs[l] : 0.0;
+#pragma unroll
+      for (int o = 1; o < kSampleThreads / 32; o <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, v, o);
+        if (l >= o) v += y;
+      }
+      if (l < kSampleThreads / 32) wscan[l] = v;
+    }
+    __syncthreads();
+    const double incl = (w > 0 ? wscan[w - 1] : 0.0) + x;
+    if (l == 31) last_incl[w] = incl;
+    __syncthreads();
+    double excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    if (l == 0) excl = w > 0 ? last_incl[w - 1] : 0.0;
+    const double total = last_incl[kSampleThreads / 32 - 1];
+    const U4 r = philox4x32_10(U4{static_cast<uint32_t>(row), static_cast<uint32_t>(p.offset),
+                                  static_cast<uint32_t>(p.offset >> 32), 0x5A3u},
+                               static_cast<uint32_t>(p.seed), static_cast<uint32_t>(p.seed >> 32));
+    double target = u53(r.x, r.y) * total;
+    if (target >= total) target = nextafter(total, 0.0);
+    int mine = 0x7fffffff;
+    if (excl <= target && target < incl) {  // this thread's slice: walk it
+      const double local = target - excl;
+      double acc = 0.0;
+      int last_nz = 0x7fffffff;
+      for (int j = threadIdx.x; j < p.V; j += kSampleThreads) {
+        const double q = q64(j);
+        acc += q;
+        if (q > 0.0) last_nz = j;
+        if (local < acc) {
+          mine = j;
+          break;
+        }
+      }
+      if (mine == 0x7fffffff) mine = last_nz;  // the local offset rounded past the slice
+    }
+    // the smallest claimed index (slices only overlap through rounding)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mine = min(mine, __shfl_xor_sync(0xffffffffu, mine, o));
+    if (l == 0) ri[w] = mine;
+    __syncthreads();
+    mine = l < kSampleThreads / 32 ? ri[l] : 0x7fffffff;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) mine = min(mine, __shfl_xor_sync(0xffffffffu, mine, o));
+    pick = mine;
+  }
+  if (threadIdx.x == 0) p.out[static_cast<long long>(b) * p.S + i] = pick;
+}
+
+}  // namespace bd3

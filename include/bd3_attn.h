@@ -165,14 +165,33 @@ BD3_API int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int6
                                void* q_out, void* k_cache, void* v_cache, const int64_t* strides,
                                int64_t cache_row0, int64_t cache_rows, int dtype, void* stream);
 
+/* One ancestral step of the BD3-LM block sampler: SUBS log-probabilities, the update weights
+ * and the float64 Gumbel-max draw, fused. Replaces subs_parameterization (model/subs.py:11-43),
+ * the step's q = exp(log_probs).double() * (1 - s/t), q[..., mask_index] = s/t,
+ * sample_categorical (sample/sampler.py:11-34) and torch.where(block != mask_index, block,
+ * new) (sample/sampler.py:114-122).
+ *   logits: (B, S, V) in dtype (BD3_BF16 or BD3_F32; with fp16 logits the reference's SUBS
+ *           raises, -1e6 overflowing fp16), vocab contiguous;
+ *           logit_strides[2] = (batch, seq) in elements. The SUBS log-softmax rounds every
+ *           op to that dtype, as the reference's tensors of that dtype do.
+ *   xt: device int64 (B, S) tokens; out: device int64 (B, S) next tokens (may alias xt).
+ *   t, s: the step's times (t > 0). Tokens that are not mask_index are kept.
+ *   uniforms: NULL to draw u with Philox4x32-10 keyed by `seed` (counter: pair index, row,
+ *   offset), or a device float64 (B, S, V) contiguous tensor of uniforms in [0, 1) to
+ *   replay a given draw (the reference's torch.rand_like). */
+BD3_API int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B,
+                            int64_t S, int64_t V, const int64_t* xt, int64_t mask_index,
+                            double t, double s, uint64_t seed, uint64_t offset,
+                            const double* uniforms, int64_t* out, int dtype, void* stream);
+
 /* ---------------------------------------------------------------------------------------
  * Per-kernel timing for benchmarks. While enabled, every launch is bracketed by a pair of
  * CUDA events on its own stream (at most 8192 launches are kept). bd3_profile_collect()
  * waits for them and writes, per kernel id (0 training forward, 1 prefill forward, 2 backward
- * prep, 3 dQ convert, 4 fused backward, 5 decode, 6 decode combine, 7 QKV RoPE cache write),
- * the summed milliseconds
+ * prep, 3 dQ convert, 4 fused backward, 5 decode, 6 decode combine, 7 QKV RoPE cache write,
+ * 8 sampler step), the summed milliseconds
  * and launch counts to
- * total_ms[8] and counts[8]; it returns 8 and forgets the recorded launches.
+ * total_ms[9] and counts[9]; it returns 9 and forgets the recorded launches.
  */
 BD3_API int bd3_profile_enable(int on);
 BD3_API int bd3_profile_collect(double* total_ms, int32_t* counts);

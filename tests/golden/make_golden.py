@@ -8,7 +8,8 @@ It imports the reference's own ``model/bd3lm.py:block_diff_mask`` (:10-52) and
 ``model/modules.py:scaled_dot_product_attention`` (:738-771), runs them on seeded
 inputs on the CPU, and writes ``tests/golden/golden.npz``; ``kv_cases`` does the same for
 ``model/modules.py:RoPE`` (:164-240) and ``model/kv_cache.py:KVCache`` (:9-55) into
-``tests/golden/golden_kv.npz``. Inputs are bf16-valued (the
+``tests/golden/golden_kv.npz``; ``sampler_cases`` runs the sampler's denoising step
+(``model/subs.py``, ``sample/sampler.py``) into ``tests/golden/golden_sampler.npz``. Inputs are bf16-valued (the
 dtype of the CUDA path) and stored as raw bf16 bits; reference outputs are stored in fp32,
 exactly as the reference returns them for fp32 inputs. The tests read only the .npz; the
 reference is not needed to run them.
@@ -108,6 +109,7 @@ def main(ref_root: str) -> None:
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
     kv_cases(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_kv.npz"))
+    sampler_cases(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden_sampler.npz"))
 
 
 # (dtype, seq, positions) for the reference's RoPE on (1, 2, seq, 64) activations
@@ -147,6 +149,43 @@ def kv_cases(path: str) -> None:
         out[f"kv_final_l{layer}_k"] = k.numpy()
         out[f"kv_final_l{layer}_v"] = v.numpy()
     out["kv_length"] = np.array(cache.length, dtype=np.int64)
+    np.savez_compressed(path, **out)
+    print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
+
+
+
+def sampler_cases(path: str) -> None:
+    """One ancestral step of sample/sampler.py:100-122 through the reference's own
+    subs_parameterization (model/subs.py:11-43) and sample_categorical (sample/sampler.py:11-34)
+    on seeded logits; the step's uniforms are replayed by reseeding torch's generator before
+    torch.rand, which sample_categorical's torch.rand_like draws from identically."""
+    from model.subs import subs_parameterization  # noqa: E402
+    from sample.sampler import sample_categorical  # noqa: E402
+
+    out = {}
+    gen = torch.Generator().manual_seed(2024)
+    B, S, V, mask = 2, 8, 1000, 999
+    # (fp16 logits make the reference's SUBS raise: -1e6 does not fit in fp16)
+    for dt, (t, s) in (("f32", (0.75, 0.5)), ("bf16", (1.0, 0.9375)), ("f32", (0.5, 0.0))):
+        tag = dt if dt == "bf16" or s else "f32_last"
+        logits = (3 * torch.randn((B, S, V), generator=gen)).to(_TORCH_DT[dt])
+        xt = torch.randint(0, V - 1, (B, S), generator=gen)
+        xt[torch.rand((B, S), generator=gen) < 0.6] = mask
+        log_probs = subs_parameterization(logits, xt, mask)
+        q = torch.exp(log_probs).double() * (1 - s / t)
+        q[..., mask] = s / t
+        torch.manual_seed(77)
+        new = sample_categorical(q)
+        torch.manual_seed(77)
+        u = torch.rand(q.shape, dtype=torch.float64)
+        nxt = torch.where(xt != mask, xt, new)
+        out[f"{tag}_logits"] = logits.float().numpy()
+        out[f"{tag}_xt"] = xt.numpy()
+        out[f"{tag}_ts"] = np.array([t, s], dtype=np.float64)
+        out[f"{tag}_u"] = u.numpy()
+        out[f"{tag}_q"] = q.numpy()
+        out[f"{tag}_next"] = nxt.numpy()
+    out["mask_index"] = np.array(mask, dtype=np.int64)
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
 
