@@ -822,8 +822,19 @@ int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B,
   const unsigned blocks = static_cast<unsigned>(B * S);
   {
     ProfScope ps(kPfSample, st);
-    if (dtype == BD3_BF16) bd3::subs_sample_kernel<0><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
-    else bd3::subs_sample_kernel<2><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    // bf16 rows up to 100,000 entries are staged in shared memory (two CTAs per SM)
+    constexpr size_t kMaxStage = 200016;
+    const size_t stage = static_cast<size_t>(V) * 2 + 16;
+    if (dtype == BD3_BF16 && stage <= kMaxStage) {
+      auto kern = bd3::subs_sample_kernel<0, true>;
+      if (const int rc = set_smem(kern, static_cast<uint32_t>(kMaxStage), 16); rc != BD3_OK)
+        return rc;
+      kern<<<blocks, bd3::kSampleThreads, stage, st>>>(p);
+    } else if (dtype == BD3_BF16) {
+      bd3::subs_sample_kernel<0, false><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    } else {
+      bd3::subs_sample_kernel<2, false><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    }
   }
   return check_launch("subs_sample_kernel launch");
 }

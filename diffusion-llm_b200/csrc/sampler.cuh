@@ -107,8 +107,12 @@ __device__ __forceinline__ void best_of(double& s, int& i, double s2, int i2) {
   if (s2 > s || (s2 == s && i2 < i)) s = s2, i = i2;
 }
 
-template <int kDtype>
+// kStage: the row is first copied into shared memory with 16-byte loads (a scalar head up to
+// the first 16-byte boundary, then whole pieces, then a scalar tail), and the three passes
+// read it from there; the element order of every pass is the same either way.
+template <int kDtype, bool kStage>
 __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const SampleParams p) {
+  extern __shared__ __align__(16) uint16_t srow_raw[];
   __shared__ float red[kSampleThreads / 32];
   __shared__ double rs[kSampleThreads / 32];
   __shared__ double wscan[kSampleThreads / 32];
@@ -123,13 +127,47 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   }
   const void* lrow = reinterpret_cast<const uint8_t*>(p.logits) +
                      (b * p.l_sb + i * p.l_ss) * (kDtype == 2 ? 4 : 2);
+  // staged rows: element j at srow_raw[j + shift], shift making the global 16-byte pieces
+  // land on 16-byte shared-memory boundaries
+  int shift = 0;
+  if constexpr (kStage) {
+    static_assert(kDtype != 2, "staging holds 16-bit rows");
+    const uint16_t* g16 = reinterpret_cast<const uint16_t*>(lrow);
+    const int head = min(p.V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(g16) & 15u)) & 15u) >> 1));
+    shift = (8 - head) & 7;
+    const int body = (p.V - head) >> 3;  // whole 16-byte pieces after the head
+    if (threadIdx.x < head) srow_raw[threadIdx.x + shift] = g16[threadIdx.x];
+    const uint4* src = reinterpret_cast<const uint4*>(g16 + head);
+    uint4* dst = reinterpret_cast<uint4*>(srow_raw + head + shift);
+    for (int c = threadIdx.x; c < body; c += 4 * kSampleThreads) {
+      uint4 v[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (c + k * kSampleThreads < body) v[k] = src[c + k * kSampleThreads];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (c + k * kSampleThreads < body) dst[c + k * kSampleThreads] = v[k];
+    }
+    for (int j = head + 8 * body + threadIdx.x; j < p.V; j += kSampleThreads)
+      srow_raw[j + shift] = g16[j];
+    __syncthreads();
+  }
+  auto logit = [&](int j) -> float {
+    if constexpr (kStage) {
+      const uint16_t h = srow_raw[j + shift];
+      if constexpr (kDtype == 0) return __uint_as_float(static_cast<uint32_t>(h) << 16);
+      else return __half2float(__ushort_as_half(h));
+    } else {
+      return logit_at<kDtype>(lrow, j);
+    }
+  };
   const int mask = static_cast<int>(p.mask_index);
   const float bias = rnd<kDtype>(-1e6f);  // model/subs.py:8
   // pass 1: max and sum of exp(x - max) of the biased logits; kUnroll independent loads in
   // flight per thread
   constexpr int kUnroll = 8;
   auto biased = [&](int j) {
-    const float x = logit_at<kDtype>(lrow, j);
+    const float x = logit(j);
     return j == mask ? rnd<kDtype>(x + bias) : x;
   };
   float mx = -INFINITY;
@@ -162,7 +200,7 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   // mask_index), then one draw.
   auto q64 = [&](int j) -> double {
     if (j == mask) return p.stay;
-    const float lp = rnd<kDtype>(rnd<kDtype>(logit_at<kDtype>(lrow, j) - mx) - lse);
+    const float lp = rnd<kDtype>(rnd<kDtype>(logit(j) - mx) - lse);
     return static_cast<double>(rnd<kDtype>(expf(lp))) * p.keep;
   };
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -237,17 +275,24 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     double target = u53(r.x, r.y) * total;
     if (target >= total) target = nextafter(total, 0.0);
     int mine = 0x7fffffff;
-    if (excl <= target && target < incl) {  // this thread's slice: walk it
-      const double local = target - excl;
+    if (excl <= target && target < incl) {  // this thread's slice: walk it, kUnroll weights
+      const double local = target - excl;  // loaded at a time, added in the same order as part
       double acc = 0.0;
       int last_nz = 0x7fffffff;
-      for (int j = threadIdx.x; j < p.V; j += kSampleThreads) {
-        const double q = q64(j);
-        acc += q;
-        if (q > 0.0) last_nz = j;
-        if (local < acc) {
-          mine = j;
-          break;
+      for (int j = threadIdx.x; j < p.V && mine == 0x7fffffff; j += kUnroll * kSampleThreads) {
+        double q[kUnroll];
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+          const int jj = j + k * kSampleThreads;
+          q[k] = jj < p.V ? q64(jj) : 0.0;
+        }
+#pragma unroll
+        for (int k = 0; k < kUnroll; ++k) {
+          const int jj = j + k * kSampleThreads;
+          if (mine != 0x7fffffff || jj >= p.V) continue;
+          acc += q[k];
+          if (q[k] > 0.0) last_nz = jj;
+          if (local < acc) mine = jj;
         }
       }
       if (mine == 0x7fffffff) mine = last_nz;  // the local offset rounded past the slice
