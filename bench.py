@@ -342,6 +342,8 @@ def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
     kc = torch.zeros(B, Hh, max_pos, Dd, dtype=torch.bfloat16, device=dev)
     vc = torch.zeros_like(kc)
     q_out = torch.empty(B, Hh, S, Dd, dtype=torch.bfloat16, device=dev)
+    for _ in range(3):
+        ops.qkv_rope_cache_raw(qkv, Hh, cos, sin, kc, vc, L, pos0=L, q_out=q_out)
     ours = statistics.median(time_steps(
         lambda: ops.qkv_rope_cache_raw(qkv, Hh, cos, sin, kc, vc, L, pos0=L, q_out=q_out),
         reps, l2))
@@ -627,11 +629,19 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
+    ap.add_argument("--extra", choices=("kv_cache", "sampler"),
+                    help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.decode_only:
         run_decode_only(args)
+    elif args.extra:
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+        fn = kv_cache_extras if args.extra == "kv_cache" else sampler_extras
+        print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)
 
