@@ -15,6 +15,8 @@ SPLIT_CASES = [  # (B, H, q_len, kv_len, bs)
     (1, 12, 16, 16, 16), (1, 12, 16, 1040, 16), (2, 3, 16, 4112, 16), (1, 2, 16, 300, 16),
     (1, 2, 40, 200, 16), (1, 2, 64, 1000, 16), (2, 2, 7, 129, 4), (1, 1, 1, 1, 1),
     (1, 2, 33, 64, 32), (3, 2, 16, 16400, 16),
+    (1, 4, 1, 70000, 16),  # one query row over a long cache (15 of the tile's rows padding)
+    (2, 2, 64, 64, 64),    # the largest decode tile, no cache before the block
 ]
 
 

@@ -13,6 +13,8 @@ pytestmark = pytest.mark.gpu
 CASES = [  # (B, H, n, block_size)
     (1, 1, 128, 16), (1, 2, 128, 4), (2, 1, 256, 16), (1, 2, 256, 128), (1, 1, 512, 64),
     (1, 1, 256, 256), (1, 2, 1024, 16), (1, 1, 1024, 4), (1, 1, 384, 32), (1, 1, 512, 1024 // 2),
+    (1, 1, 128, 1),      # one-token blocks: the densest rule pattern
+    (1, 1, 2048, 64), (1, 1, 4096, 128),  # long sequences (2n = 4096, 8192)
 ]
 
 
@@ -39,7 +41,8 @@ def test_forward_matches_oracle(B, H, n, bs):
     assert_close("LSE", lse, ref_lse, LSE_TOL)
 
 
-@pytest.mark.parametrize("B,H,n,bs", [c for c in CASES if c[2] <= 512] + [(1, 1, 1024, 16)])
+@pytest.mark.parametrize("B,H,n,bs", [c for c in CASES if c[2] <= 512] + [(1, 1, 1024, 16),
+                                                                          (1, 1, 2048, 64)])
 def test_backward_matches_oracle(B, H, n, bs):
     (q, k, v, do), (o, dq, dk, dv) = _run(B, H, n, bs, seed=2)
     mask = oracle.block_diff_mask(n, bs)
