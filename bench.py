@@ -324,6 +324,28 @@ def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """BASELINE config 4 alone (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per
+    (b, h)), as decode_extras times it: the command the live-block ncu capture runs."""
+    from bd3attn import ops
+    g = torch.Generator().manual_seed(5)
+    b4, kv4, nb, live = 16, 8192, 128, 32
+    q4 = torch.randn(b4, H, 16, D, generator=g).bfloat16().to(dev)
+    k4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
+    v4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
+    idx = torch.stack([torch.cat([torch.randperm(nb - 1, generator=g)[:live - 1].sort().values,
+                                  torch.tensor([nb - 1])]) for _ in range(b4 * H)])
+    idx = idx.view(b4, H, live).int().to(dev)
+    cnt = torch.full((b4, H), live, dtype=torch.int32, device=dev)
+    for _ in range(3):
+        ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS)
+    ms = time_steps(lambda: ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS), reps, l2)
+    by = b4 * H * (live * 64 * 256 + 4096)
+    t = statistics.median(ms)
+    return {"live_b16_kv8k_25pct": {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
+                                    "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}}
+
+
 def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
     """The cached-sampling K/V path (SURVEY next row 1) at the generation config (B=64,
     H=12, head_dim 64, 16-token blocks, max_seq_len 1024): one layer of one denoising step of
@@ -629,7 +651,7 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
-    ap.add_argument("--extra", choices=("kv_cache", "sampler"),
+    ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -640,7 +662,8 @@ def main():
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
-        fn = kv_cache_extras if args.extra == "kv_cache" else sampler_extras
+        fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
+              "live_decode": live_decode_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)
