@@ -124,8 +124,7 @@ class KVCache:
         n = self._len[layer_idx]
         self._reserve(layer_idx, B, n_heads, D, qkv.dtype, qkv.device, n + S)
         kc, vc = self._k[layer_idx], self._v[layer_idx]
-        q = ops.qkv_rope_cache_raw(qkv, n_heads, cos_table, sin_table, kc, vc, n,
-                                   positions=positions, pos0=0)
+        q = ops.qkv_rope_cache_op(qkv, n_heads, cos_table, sin_table, kc, vc, n, positions)
         if store:
             self._len[layer_idx] = n + S
         return q, kc[:, :, :n + S], vc[:, :, :n + S]

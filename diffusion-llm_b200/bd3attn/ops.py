@@ -254,6 +254,21 @@ def qkv_rope_cache_raw(qkv, n_heads: int, cos_table, sin_table, k_cache, v_cache
     return q_out
 
 
+@torch.library.custom_op("bd3::qkv_rope_cache", mutates_args=("k_cache", "v_cache"))
+def qkv_rope_cache_op(qkv: torch.Tensor, n_heads: int, cos_table: torch.Tensor,
+                      sin_table: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                      row0: int, positions: torch.Tensor | None = None) -> torch.Tensor:
+    """qkv_rope_cache_raw as a custom op: writes the caches in place, returns q."""
+    return qkv_rope_cache_raw(qkv, n_heads, cos_table, sin_table, k_cache, v_cache, row0,
+                              positions=positions)
+
+
+@qkv_rope_cache_op.register_fake
+def _(qkv, n_heads, cos_table, sin_table, k_cache, v_cache, row0, positions=None):
+    B, S, F = qkv.shape
+    return qkv.new_empty((B, n_heads, S, F // (3 * n_heads)))
+
+
 # ---------------------------------------------------------------------------------------
 PROFILE_KERNELS = ("attn_fwd", "attn_prefill", "bwd_prep", "bwd_dq_convert", "bwd_fused",
                    "decode", "decode_combine", "qkv_rope_cache", "subs_sample")
