@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the BD3-LM attention hot path on B200 (one JSON line on rank 0).
 
-Headline workload: BD3-LM training attention forward + backward,
+Headline workload (benchmark config 2): BD3-LM training attention forward + backward,
 B=8 per GPU, H=12, n=1024 per half (2n = 2048), head_dim 64, bf16, block_size 16, synthetic
 N(0,1) inputs from a seed. A step is one forward (O, LSE) and one backward (dQ, dK, dV)
 through the C ABI with the inputs resident in HBM; before every step a 256 MiB buffer is
@@ -293,7 +293,7 @@ def time_steps(fn, steps: int, l2) -> list[float]:
 
 
 def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
-    """Decode rows of BASELINE configs 3 and 4 (HBM-bound): time and achieved GB/s."""
+    """Decode rows of benchmark configs 3 and 4 (HBM-bound): time and achieved GB/s."""
     out = {}
     g = torch.Generator().manual_seed(5)
     # C3: split-KV, B=32, H=12, q_len=16, cache 64K + the block itself
@@ -325,7 +325,7 @@ def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
 
 
 def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
-    """BASELINE config 4 alone (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per
+    """Benchmark config 4 alone (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per
     (b, h)), as decode_extras times it: the command the live-block ncu capture runs."""
     from bd3attn import ops
     g = torch.Generator().manual_seed(5)
@@ -347,7 +347,7 @@ def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
 
 
 def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
-    """The cached-sampling K/V path (SURVEY next row 1) at the generation config (B=64,
+    """The cached-sampling K/V path at the generation config (B=64,
     H=12, head_dim 64, 16-token blocks, max_seq_len 1024): one layer of one denoising step of
     the last block (1008 cached tokens), through bd3_qkv_rope_cache (q out, k/v written in
     place) beside the reference's ops for the same step (model/modules.py:395-417: rearrange,
@@ -401,8 +401,58 @@ def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def graph_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """The attention side of one denoising step of cached sampling at batch 1 (12 layers,
+    H=12, head_dim 64, a 16-token block after 1008 cached tokens): per layer the fused
+    QKV/RoPE cache write and the split-KV decode, issued eagerly through the Python API and
+    replayed as one CUDA graph captured once (cache rows from the device positions, key count
+    from a device int32, so the same graph serves every block). At batch 1 each kernel runs
+    for microseconds and the eager step is bound by launch overhead."""
+    from bd3attn import ops
+    layers, Bb, S, cap, L = 12, 1, 16, 1024, 1008
+    pos_t = torch.arange(cap, dtype=torch.float64)
+    inv = 10000.0 ** (-torch.arange(0, D, 2, dtype=torch.float64) / D)
+    ang = pos_t[:, None] * inv[None, :]
+    sin, cos = torch.sin(ang).float().to(dev), torch.cos(ang).float().to(dev)
+    g = torch.Generator().manual_seed(9)
+    x = [torch.randn(Bb, S, 3 * H * D, generator=g).bfloat16().to(dev) for _ in range(layers)]
+    caches = [(torch.randn(Bb, H, cap, D, generator=g).bfloat16().to(dev),
+               torch.randn(Bb, H, cap, D, generator=g).bfloat16().to(dev)) for _ in range(layers)]
+    q_buf = [torch.empty(Bb, H, S, D, dtype=torch.bfloat16, device=dev) for _ in range(layers)]
+    pos = torch.arange(L, L + S, device=dev)
+    kv_len = torch.tensor([L + S], dtype=torch.int32, device=dev)
+
+    def step():
+        outs = []
+        for i, (kc, vc) in enumerate(caches):
+            q = ops.qkv_rope_cache_raw(x[i], H, cos, sin, kc, vc, -1, positions=pos,
+                                       q_out=q_buf[i])
+            outs.append(ops.decode_raw(q, kc, vc, BS, kv_len_dev=kv_len))
+        return outs
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    eager = statistics.median(time_steps(step, reps, l2))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        graph.replay()
+    replay = statistics.median(time_steps(graph.replay, reps, l2))
+    del graph
+    ns, _ = ops.decode_plan(Bb, H, S, cap, BS)
+    per_layer = 2 + (1 if ns > 1 else 0)  # RoPE/cache write, decode, combine when split
+    return {"decode_step_12_layers_b1": {"eager_us": round(eager * 1e3, 2),
+                                         "graph_us": round(replay * 1e3, 2),
+                                         "kernels": per_layer * layers, "n_splits": ns}}
+
+
 def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
-    """One denoising step of the block sampler (SURVEY next row 2) at the generation config:
+    """One denoising step of the block sampler at the generation config:
     B=64 sequences, a 16-token block, vocabulary 50258, bf16 logits (the backbone runs under
     autocast), every token still masked (a block's first step). bd3_subs_sample beside the
     reference's ops for the same step (model/subs.py:11-43, sample/sampler.py:11-34, 100-122:
@@ -651,7 +701,7 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
-    ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode"),
+    ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -663,7 +713,7 @@ def main():
         dev = torch.device("cuda", 0)
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
         fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
-              "live_decode": live_decode_extras}[args.extra]
+              "live_decode": live_decode_extras, "graph_step": graph_step_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)

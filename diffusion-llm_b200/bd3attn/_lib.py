@@ -34,6 +34,8 @@ SIGNATURES = {
     "bd3_decode_plan": (_i32, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _psz]),
     "bd3_decode_attn": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64,
                                _i64, _i64, _i64, _i64, _i32, _i32, _vp, _sz, _vp]),
+    "bd3_decode_attn_devlen": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
+                                      _pi64, _i64, _vp, _i64, _i32, _i32, _vp, _sz, _vp]),
     "bd3_decode_attn_noalloc": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
                                        _pi64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "bd3_decode_live_plan": (_i32, [_i64, _i64, _i64, _i64, _i64, _pi64, _psz]),

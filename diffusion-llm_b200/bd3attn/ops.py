@@ -97,13 +97,22 @@ def decode_plan(B, H, q_len, kv_len, block_size, q_pos0=-1, kv_pos0=0):
 
 
 def decode_raw(q, k, v, block_size: int, q_pos0: int = -1, kv_pos0: int = 0,
-               out_dtype=None, return_lse: bool = False, n_splits: int | None = None):
-    """Block-causal decode attention of the q_len queries over kv_len keys."""
+               out_dtype=None, return_lse: bool = False, n_splits: int | None = None,
+               kv_len_dev=None):
+    """Block-causal decode attention of the q_len queries over kv_len keys.
+
+    kv_len_dev: an int32 device tensor of one element holding the key count; k and v are then
+    the whole cache storage (B, H, capacity, 64), the queries sit at the count's end and
+    q_pos0 / kv_pos0 / n_splits are ignored. The launch does not depend on the count, so a
+    CUDA graph captured around it replays every step of a growing cache.
+    """
     _check_cuda(q, k, v)
     q, k, v = _rows_contig(q), _rows_contig(k), _rows_contig(v)
     B, H, q_len, D = q.shape
     kv_len = k.shape[2]
     out_dtype = q.dtype if out_dtype is None else out_dtype
+    if kv_len_dev is not None:
+        return _decode_devlen(q, k, v, int(block_size), kv_len_dev, out_dtype, return_lse)
     ns, wb = decode_plan(B, H, q_len, kv_len, int(block_size), q_pos0, kv_pos0)
     if n_splits is not None and q_len <= 64:
         ns = int(n_splits)
@@ -117,6 +126,25 @@ def decode_raw(q, k, v, block_size: int, q_pos0: int = -1, kv_pos0: int = 0,
             _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, q_len, kv_len, D, strides,
             int(block_size), int(q_pos0), int(kv_pos0), ns, _code(q.dtype), _code(out_dtype),
             _ptr(ws), wb, _stream(q)))
+    return (o, lse) if return_lse else o
+
+
+def _decode_devlen(q, k, v, block_size, kv_len_dev, out_dtype, return_lse):
+    _check_cuda(kv_len_dev)
+    if kv_len_dev.dtype != torch.int32 or kv_len_dev.numel() != 1:
+        raise AssertionError("kv_len_dev must be a one-element int32 device tensor")
+    B, H, q_len, D = q.shape
+    capacity = k.shape[2]
+    ns, wb = decode_plan(B, H, q_len, capacity, block_size, -1, 0)
+    o = torch.empty((B, H, q_len, D), dtype=out_dtype, device=q.device)
+    lse = torch.empty((B, H, q_len), dtype=torch.float32, device=q.device) if return_lse else None
+    ws = torch.empty(max(wb, 16), dtype=torch.uint8, device=q.device)
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o))
+    with torch.cuda.device(q.device):
+        check("bd3_decode_attn_devlen", LIB.bd3_decode_attn_devlen(
+            _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), B, H, q_len, capacity, D, strides,
+            block_size, _ptr(kv_len_dev), ns, _code(q.dtype), _code(out_dtype), _ptr(ws), wb,
+            _stream(q)))
     return (o, lse) if return_lse else o
 
 
@@ -220,6 +248,8 @@ def qkv_rope_cache_raw(qkv, n_heads: int, cos_table, sin_table, k_cache, v_cache
     cos_table, sin_table: (max_pos, D / 2) fp32 (RoPE's buffers); k_cache, v_cache:
     (B, n_heads, rows, D) in qkv's dtype; positions: (S,) int64 absolute positions on the
     device, or None for pos0, pos0 + 1, ...; q_out: (B, n_heads, S, D) or None to allocate.
+    row0 < 0 takes the first cache row from the device value positions[0] (positions
+    required), so a captured CUDA graph writes each new block at its own rows.
     """
     _check_cuda(qkv, cos_table, sin_table, k_cache, v_cache)
     if qkv.dim() != 3:

@@ -443,7 +443,8 @@ int launch_decode(bool live, const void* q, const void* k, const void* v, void* 
                   int64_t live_stride, int64_t max_live, int64_t kv_block, int64_t B, int64_t H,
                   int64_t q_len, int64_t kv_len, const int64_t* strides, int64_t bs,
                   int64_t q_pos0, int64_t kv_pos0, int64_t n_splits, int dtype, int out_dtype,
-                  void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                  void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  const int32_t* kv_len_dev = nullptr) {
   const int kmb = q_len <= 16 ? 1 : 2;
   const int64_t groups = q_len <= 32 ? 1 : (q_len + 31) / 32;
   int rc;
@@ -467,6 +468,7 @@ int launch_decode(bool live, const void* q, const void* k, const void* v, void* 
   p.ws_lse = need > 0 ? p.ws_o + B * H * n_splits * q_len * 64 : nullptr;
   p.live_idx = live_idx;
   p.live_cnt = live_cnt;
+  p.kv_len_dev = kv_len_dev;
   p.o_sb = so[0];
   p.o_sh = so[1];
   p.o_ss = so[2];
@@ -563,6 +565,34 @@ int bd3_decode_attn(const void* q, const void* k, const void* v, void* o, float*
   return launch_decode(false, q, k, v, o, lse_out, nullptr, nullptr, 0, 0, 64, B, H, q_len,
                        kv_len, strides, block_size, q_pos0, kv_pos0, n_splits, dtype,
                        out_dtype, workspace, workspace_bytes, st);
+}
+
+// Decode over a cache whose key count lives on the device. The host plans the split count
+// and builds the tensor maps for the capacity; the kernel reads the count, places the
+// queries at its end and spreads the key tiles over the splits (decode_kernel), so the
+// launch arguments stay the same while the cache grows and one captured CUDA graph replays
+// every step of a sampling loop.
+int bd3_decode_attn_devlen(const void* q, const void* k, const void* v, void* o,
+                           float* lse_out, int64_t B, int64_t H, int64_t q_len,
+                           int64_t kv_capacity, int64_t D, const int64_t* strides,
+                           int64_t block_size, const int32_t* kv_len_dev, int64_t n_splits,
+                           int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  if (kv_len_dev == nullptr) return fail(BD3_ERR_INVALID, "kv_len_dev is required");
+  if (q_len < 1 || q_len > 64)
+    return fail(BD3_ERR_UNSUPPORTED, "device-length decode handles 1 <= q_len <= 64 (got %lld)",
+                (long long)q_len);
+  if (kv_capacity < q_len || kv_capacity > (1LL << 30))
+    return fail(BD3_ERR_INVALID, "kv_capacity must be in [q_len, 2^30]");
+  if (block_size < 1) return fail(BD3_ERR_INVALID, "block_size must be >= 1");
+  if (out_dtype != dtype && out_dtype != BD3_F32)
+    return fail(BD3_ERR_INVALID, "out_dtype must equal dtype or be fp32");
+  const int rc = check_dims(B, H, D, dtype);
+  if (rc != BD3_OK) return rc;
+  return launch_decode(false, q, k, v, o, lse_out, nullptr, nullptr, 0, 0, 64, B, H, q_len,
+                       kv_capacity, strides, block_size, kv_capacity - q_len, 0, n_splits,
+                       dtype, out_dtype, workspace, workspace_bytes,
+                       static_cast<cudaStream_t>(stream), kv_len_dev);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -734,7 +764,10 @@ int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, i
   if (positions == nullptr && (pos0 < 0 || pos0 + S > max_pos))
     return fail(BD3_ERR_INVALID, "positions [%lld, %lld) outside the RoPE table of %lld rows",
                 (long long)pos0, (long long)(pos0 + S), (long long)max_pos);
-  if (cache_row0 < 0 || cache_row0 + S > cache_rows)
+  if (cache_row0 < 0 && positions == nullptr)
+    return fail(BD3_ERR_INVALID, "cache_row0 < 0 takes the cache row from positions[0]: "
+                "positions is required");
+  if (S > cache_rows || (cache_row0 >= 0 && cache_row0 + S > cache_rows))
     return fail(BD3_ERR_INVALID, "cache rows [%lld, %lld) outside a cache of %lld rows",
                 (long long)cache_row0, (long long)(cache_row0 + S), (long long)cache_rows);
   if (const int rc = ensure_context(); rc != BD3_OK) return rc;
@@ -772,6 +805,7 @@ int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, i
   p.v_cache = v_cache;
   p.v_sb = strides[6]; p.v_sh = strides[7]; p.v_ss = strides[8];
   p.row0 = cache_row0;
+  p.cache_rows = cache_rows;
   p.B = static_cast<int>(B);
   p.S = static_cast<int>(S);
   p.H = static_cast<int>(H);

@@ -31,6 +31,7 @@ struct DecParams {
   float* ws_lse;         // (B*H, n_splits, q_len)
   const int* live_idx;   // live mode: (B*H, live_stride) block indices, ascending
   const int* live_cnt;   // live mode: (B*H)
+  const int* kv_len_dev; // optional device key count (contiguous mode; see decode_kernel)
   long long o_sb, o_sh, o_ss;
   int H;
   int q_len, kv_len;
@@ -122,7 +123,26 @@ template <int kMB, bool kBF16, bool kLive>
 __global__ void __launch_bounds__(kDecThreads)
     decode_kernel(const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const DecParams p) {
+                  const __grid_constant__ CUtensorMap tm_v, const DecParams p_in) {
+  // With kv_len_dev the key count is read on the device (kv_len is then the cache capacity
+  // the tensor maps and the split count were built for): the queries are the last q_len of
+  // those keys, key 0 at position 0, and the key tiles are spread over all n_splits again.
+  // A count outside [q_len, capacity] is clamped and raises status bit 2. A CUDA graph
+  // captured once thus serves a cache that grows between replays.
+  DecParams p = p_in;
+  if (!kLive && p.kv_len_dev != nullptr) {
+    int kl = *p.kv_len_dev;
+    if (kl < p.q_len || kl > p.kv_len) {
+      if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+        atomicOr(&g_bd3_status, kStatusBadLaunch);
+      kl = kl < p.q_len ? p.q_len : p.kv_len;
+    }
+    p.kv_len = kl;
+    p.q_pos0 = kl - p.q_len;
+    p.kv_pos0 = 0;
+    const int tiles = cdiv(kl, kDecBN);
+    p.tiles_per_split = tiles > p.n_splits ? cdiv(tiles, p.n_splits) : 1;
+  }
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);

@@ -41,7 +41,8 @@ struct RopeCacheParams {
   long long k_sb, k_sh, k_ss;
   void* v_cache;
   long long v_sb, v_sh, v_ss;
-  long long row0;                  // cache row of token s = 0
+  long long row0;                  // cache row of token s = 0; < 0: positions[0] (device)
+  long long cache_rows;            // rows of each cache (bounds the row read from positions)
   int B, S, H, D;
 };
 
@@ -93,6 +94,14 @@ __global__ void __launch_bounds__(256) qkv_rope_cache_kernel(const RopeCachePara
   const int s = static_cast<int>(u % p.S);
   const int b = static_cast<int>(u / p.S);
 
+  // A negative row0 places the tokens at cache rows positions[0] + s: the cache row then
+  // follows a position tensor that stays on the device, so one captured launch serves every
+  // block of a sampling loop. A row range outside the cache writes nothing (status bit 4).
+  const long long row0 = p.row0 >= 0 ? p.row0 : p.positions[0];
+  if (row0 < 0 || row0 + p.S > p.cache_rows) {
+    if (t == 0) atomicOr(&g_bd3_status, kStatusBadPosition);
+    return;
+  }
   const long long pos = p.positions != nullptr ? p.positions[s] : p.pos0 + s;
   if (pos < 0 || pos >= p.max_pos) {
     if (t == 0) atomicOr(&g_bd3_status, kStatusBadPosition);
@@ -106,8 +115,8 @@ __global__ void __launch_bounds__(256) qkv_rope_cache_kernel(const RopeCachePara
   const float* ct = p.cos_table + pos * half + 8 * t;
   const float* st = p.sin_table + pos * half + 8 * t;
   const long long qo = b * p.q_sb + h * p.q_sh + s * p.q_ss;
-  const long long ko = b * p.k_sb + h * p.k_sh + (p.row0 + s) * p.k_ss;
-  const long long vo = b * p.v_sb + h * p.v_sh + (p.row0 + s) * p.v_ss;
+  const long long ko = b * p.k_sb + h * p.k_sh + (row0 + s) * p.k_ss;
+  const long long vo = b * p.v_sb + h * p.v_sh + (row0 + s) * p.v_ss;
   const int k = 8 * t;
   float c[8], sn[8];
   {

@@ -100,6 +100,22 @@ BD3_API int bd3_decode_attn(const void* q, const void* k, const void* v, void* o
                     int64_t n_splits, int dtype, int out_dtype, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Decode over a KV cache whose key count is a device int32 (*kv_len_dev), so the launch
+ * arguments do not change as the cache grows and one captured CUDA graph replays every
+ * denoising step. The same attention as bd3_decode_attn with the reference's placement (the
+ * queries are the last q_len of the *kv_len_dev keys, kv_pos0 = 0); the reference's
+ * kernels/SplitKVDecodeAttention.py:130-171 reads the count from k.shape instead.
+ *   k, v: (B, H, kv_capacity, 64) cache storage (rows past the count are never read).
+ *   n_splits, workspace: from bd3_decode_plan(B, H, q_len, kv_capacity, block_size, -1, 0).
+ * A count outside [q_len, kv_capacity] is clamped into it and sets device status bit 2.
+ * q_len <= 64; the other arguments are those of bd3_decode_attn. */
+BD3_API int bd3_decode_attn_devlen(const void* q, const void* k, const void* v, void* o,
+                                   float* lse_out, int64_t B, int64_t H, int64_t q_len,
+                                   int64_t kv_capacity, int64_t D, const int64_t* strides,
+                                   int64_t block_size, const int32_t* kv_len_dev,
+                                   int64_t n_splits, int dtype, int out_dtype, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
 /* Decode without allocation: the same result as bd3_decode_attn (split count from
  * bd3_decode_plan) for callers that cannot call cudaMalloc, such as a serving engine whose
  * allocator owns all device memory, or a decode loop that must not take the synchronisation
@@ -158,7 +174,10 @@ BD3_API int bd3_lse_merge(const float* parts, const float* lses, void* o, float*
  *   strides[9] = q_out, k_cache, v_cache (batch, head, seq) in elements.
  * dtype: BD3_BF16, BD3_F16 or BD3_F32 (all tensors but the tables). head_dim % 16 == 0;
  * pointers and strides 16-byte aligned. A device position outside [0, max_pos) (the
- * reference raises IndexError) leaves its token unwritten and sets device status bit 4. */
+ * reference raises IndexError) leaves its token unwritten and sets device status bit 4.
+ * cache_row0 < 0 takes the first cache row from the device value positions[0] (positions
+ * required), so a CUDA graph captured once writes each new block at its own rows; a row
+ * range outside [0, cache_rows) then writes nothing and sets status bit 4. */
 BD3_API int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, int64_t S,
                                int64_t H, int64_t D, const int64_t* positions, int64_t pos0,
                                const float* cos_table, const float* sin_table, int64_t max_pos,

@@ -82,3 +82,24 @@ def test_library_tile_sizes_cover_masks():
     assert (bm, bn) in {(128, 64), (128, 128)}
     assert (bkv, bq) in {(128, 32), (128, 64), (128, 128)}
     assert dec_bn == 64 and dq_bm == 128
+
+
+def _devlen(**over):
+    """bd3_decode_attn_devlen with plausible arguments (fake non-null pointers: each case
+    below is rejected before the library touches memory or CUDA)."""
+    from bd3attn._lib import LIB, i64_array
+    a = dict(B=1, H=2, q_len=16, cap=256, kv_len_dev=0x5000, out_dtype=0)
+    a.update(over)
+    return LIB.bd3_decode_attn_devlen(0x1000, 0x2000, 0x3000, 0x4000, None, a["B"], a["H"],
+                                      a["q_len"], a["cap"], 64, i64_array([0] * 12), 16,
+                                      a["kv_len_dev"], 1, 0, a["out_dtype"], None, 0, None)
+
+
+def test_capi_devlen_decode_argument_checks():
+    from bd3attn._lib import BD3_ERR_INVALID, BD3_ERR_UNSUPPORTED, LIB
+    assert _devlen(kv_len_dev=None) == BD3_ERR_INVALID
+    assert "kv_len_dev" in LIB.bd3_last_error().decode()
+    assert _devlen(q_len=65) == BD3_ERR_UNSUPPORTED
+    assert _devlen(q_len=0) == BD3_ERR_UNSUPPORTED
+    assert _devlen(cap=8) == BD3_ERR_INVALID       # capacity below the query block
+    assert _devlen(out_dtype=1) == BD3_ERR_INVALID  # bf16 in, fp16 out

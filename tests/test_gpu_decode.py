@@ -185,7 +185,7 @@ def test_live_blocks_long_list_single_split():
 
 
 def test_full_config3_size():
-    """BASELINE config 3 at its largest single-GPU size (B=32, H=12, q_len 16, a 64K cache
+    """Benchmark config 3 at its largest single-GPU size (B=32, H=12, q_len 16, a 64K cache
     plus the block itself): the planned split-KV decode equals the oracle on two (b, h)
     slices, and equals the LSE merge of two sequence-shard decodes of the same cache (a
     size-independent consistency check over all 384 (b, h) pairs)."""

@@ -106,7 +106,7 @@ def test_fp16_inputs():
 
 
 def test_fp32_inputs_config1_shape():
-    """BASELINE config 1 (B=2, H=12, n=1024, bs=16, fp32): computed in bf16 here."""
+    """Benchmark config 1 (B=2, H=12, n=1024, bs=16, fp32): computed in bf16 here."""
     from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
     q, k, v = qkv(9, 2, 12, 2048, 2048, torch.float32)
     o = BlockSparseFlashAttention.apply(q.cuda(), k.cuda(), v.cuda(), 16)
@@ -147,7 +147,7 @@ def test_forward_with_row_divergent_rescales(bs):
 
 @pytest.mark.parametrize("bs", [4, 16])
 def test_full_config2_size_runs_clean(bs):
-    """BASELINE config 2 at full size (B=8, H=12, n=1024): repeated fwd+bwd launches finish
+    """Benchmark config 2 at full size (B=8, H=12, n=1024): repeated fwd+bwd launches finish
     with no bounded wait running out; two heads checked against the oracle."""
     from bd3attn import ops
     B, H, n = 8, 12, 1024

@@ -123,3 +123,6 @@ def test_capi_rope_cache_argument_checks():
     assert _call(pos0=-1) == BD3_ERR_INVALID
     assert _call(row0=13) == BD3_ERR_INVALID        # rows [13, 17) outside 16
     assert "cache rows" in LIB.bd3_last_error().decode()
+    assert _call(row0=-1) == BD3_ERR_INVALID        # rows from positions[0], but no positions
+    assert "positions is required" in LIB.bd3_last_error().decode()
+    assert _call(row0=-1, positions=0x7000, S=17) == BD3_ERR_INVALID  # S > cache rows
