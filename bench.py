@@ -406,9 +406,12 @@ def graph_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     H=12, head_dim 64, a 16-token block after 1008 cached tokens): per layer the fused
     QKV/RoPE cache write and the split-KV decode, issued eagerly through the Python API and
     replayed as one CUDA graph captured once (cache rows from the device positions, key count
-    from a device int32, so the same graph serves every block). At batch 1 each kernel runs
-    for microseconds and the eager step is bound by launch overhead."""
+    from a device int32, so the same graph serves every block); then the same with the
+    sampler step (vocabulary 50258, bf16 logits, (t, s) and (seed, offset) on the device)
+    appended. At batch 1 each kernel runs for microseconds and the eager step is bound by
+    launch overhead."""
     from bd3attn import ops
+    from bd3attn.sampler import subs_sample_step_dev
     layers, Bb, S, cap, L = 12, 1, 16, 1024, 1008
     pos_t = torch.arange(cap, dtype=torch.float64)
     inv = 10000.0 ** (-torch.arange(0, D, 2, dtype=torch.float64) / D)
@@ -422,33 +425,44 @@ def graph_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     pos = torch.arange(L, L + S, device=dev)
     kv_len = torch.tensor([L + S], dtype=torch.int32, device=dev)
 
-    def step():
+    V = 50258
+    logits = torch.randn(Bb, S, V, generator=g).bfloat16().to(dev)
+    block = torch.full((Bb, S), V - 1, dtype=torch.int64, device=dev)
+    ts = torch.tensor([0.5, 0.25], dtype=torch.float64, device=dev)
+    rng = torch.tensor([12345, 0], dtype=torch.int64, device=dev)
+
+    def step(with_sampler):
         outs = []
         for i, (kc, vc) in enumerate(caches):
             q = ops.qkv_rope_cache_raw(x[i], H, cos, sin, kc, vc, -1, positions=pos,
                                        q_out=q_buf[i])
             outs.append(ops.decode_raw(q, kc, vc, BS, kv_len_dev=kv_len))
+        if with_sampler:
+            outs.append(subs_sample_step_dev(logits, block, V - 1, ts, rng))
         return outs
 
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        for _ in range(3):
-            step()
-    torch.cuda.current_stream().wait_stream(side)
-    eager = statistics.median(time_steps(step, reps, l2))
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        step()
-    for _ in range(3):
-        graph.replay()
-    replay = statistics.median(time_steps(graph.replay, reps, l2))
-    del graph
     ns, _ = ops.decode_plan(Bb, H, S, cap, BS)
     per_layer = 2 + (1 if ns > 1 else 0)  # RoPE/cache write, decode, combine when split
-    return {"decode_step_12_layers_b1": {"eager_us": round(eager * 1e3, 2),
-                                         "graph_us": round(replay * 1e3, 2),
-                                         "kernels": per_layer * layers, "n_splits": ns}}
+    out = {}
+    for name, with_sampler in (("decode_step_12_layers_b1", False),
+                               ("decode_step_12_layers_and_sampler_b1", True)):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                step(with_sampler)
+        torch.cuda.current_stream().wait_stream(side)
+        eager = statistics.median(time_steps(lambda: step(with_sampler), reps, l2))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step(with_sampler)
+        for _ in range(3):
+            graph.replay()
+        replay = statistics.median(time_steps(graph.replay, reps, l2))
+        del graph
+        out[name] = {"eager_us": round(eager * 1e3, 2), "graph_us": round(replay * 1e3, 2),
+                     "kernels": per_layer * layers + int(with_sampler), "n_splits": ns}
+    return out
 
 
 def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:

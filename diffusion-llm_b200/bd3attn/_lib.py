@@ -49,6 +49,8 @@ SIGNATURES = {
     "bd3_subs_sample": (_i32, [_vp, _pi64, _i64, _i64, _i64, _vp, _i64, ctypes.c_double,
                                ctypes.c_double, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _i32,
                                _vp]),
+    "bd3_subs_sample_dev": (_i32, [_vp, _pi64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _i32,
+                                   _vp]),
     "bd3_profile_enable": (_i32, [_i32]),
     "bd3_profile_collect": (_i32, [ctypes.POINTER(ctypes.c_double), _pi32]),
     "bd3_debug_ranges": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi32]),

@@ -52,3 +52,33 @@ def subs_sample_step(logits: torch.Tensor, block: torch.Tensor, mask_index: int,
             int(mask_index), float(t), float(s), seed, int(offset), _ptr(uniforms), _ptr(out),
             _code(logits.dtype), _stream(logits)))
     return out
+
+
+def subs_sample_step_dev(logits: torch.Tensor, block: torch.Tensor, mask_index: int,
+                         ts: torch.Tensor, seed_offset: torch.Tensor,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+    """subs_sample_step's Philox draw with the step's values on the device, for a sampling
+    loop captured in a CUDA graph: ts is a float64 device tensor (t, s) and seed_offset an
+    int64 device tensor (seed, offset) read as unsigned 64-bit words. Advance them between
+    replays (for example ``seed_offset[1] += 1``); nothing here reads them on the host."""
+    _check_cuda(logits, block, ts, seed_offset)
+    if logits.dim() != 3 or block.shape != logits.shape[:2]:
+        raise AssertionError("logits must be (batch, seq, vocab) and block (batch, seq)")
+    if ts.dtype != torch.float64 or ts.numel() != 2 or not ts.is_contiguous():
+        raise AssertionError("ts must be a contiguous float64 device tensor (t, s)")
+    if seed_offset.dtype != torch.int64 or seed_offset.numel() != 2 \
+            or not seed_offset.is_contiguous():
+        raise AssertionError("seed_offset must be a contiguous int64 device tensor (seed, offset)")
+    if logits.stride(-1) != 1:
+        logits = logits.contiguous()
+    if block.dtype != torch.int64 or not block.is_contiguous():
+        raise AssertionError("block must be a contiguous int64 tensor")
+    B, S, V = logits.shape
+    if out is None:
+        out = torch.empty_like(block)
+    with torch.cuda.device(logits.device):
+        check("bd3_subs_sample_dev", LIB.bd3_subs_sample_dev(
+            _ptr(logits), i64_array((logits.stride(0), logits.stride(1))), B, S, V, _ptr(block),
+            int(mask_index), _ptr(ts), _ptr(seed_offset), _ptr(out), _code(logits.dtype),
+            _stream(logits)))
+    return out

@@ -821,10 +821,10 @@ int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, i
   return check_launch("qkv_rope_cache_kernel launch");
 }
 
-int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B, int64_t S,
-                    int64_t V, const int64_t* xt, int64_t mask_index, double t, double s,
-                    uint64_t seed, uint64_t offset, const double* uniforms, int64_t* out,
-                    int dtype, void* stream) {
+extern "C++" {  // the launcher is a template
+namespace {
+int check_sample_args(const void* logits, int64_t B, int64_t S, int64_t V, const int64_t* xt,
+                      int64_t mask_index, const int64_t* out, int dtype) {
   if (dtype != BD3_BF16 && dtype != BD3_F32)  // the reference's SUBS cannot hold -1e6 in fp16
     return fail(BD3_ERR_INVALID, "logits must be bf16 or fp32 (got dtype %d)", dtype);
   if (B < 1 || S < 1 || V < 2) return fail(BD3_ERR_INVALID, "need B, S >= 1 and V >= 2");
@@ -835,6 +835,41 @@ int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B,
                 (long long)mask_index, (long long)V);
   if (logits == nullptr || xt == nullptr || out == nullptr)
     return fail(BD3_ERR_INVALID, "logits, xt and out are required");
+  return BD3_OK;
+}
+
+template <bool kDevArgs>
+int launch_sample(const bd3::SampleParams& p, int dtype, cudaStream_t st) {
+  const unsigned blocks = static_cast<unsigned>(static_cast<int64_t>(p.B) * p.S);
+  {
+    ProfScope ps(kPfSample, st);
+    // bf16 rows up to 100,000 entries are staged in shared memory (two CTAs per SM)
+    constexpr size_t kMaxStage = 200016;
+    const size_t stage = static_cast<size_t>(p.V) * 2 + 16;
+    if (dtype == BD3_BF16 && stage <= kMaxStage) {
+      auto kern = bd3::subs_sample_kernel<0, true, kDevArgs>;
+      if (const int rc = set_smem(kern, static_cast<uint32_t>(kMaxStage), kDevArgs ? 17 : 16);
+          rc != BD3_OK)
+        return rc;
+      kern<<<blocks, bd3::kSampleThreads, stage, st>>>(p);
+    } else if (dtype == BD3_BF16) {
+      bd3::subs_sample_kernel<0, false, kDevArgs><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    } else {
+      bd3::subs_sample_kernel<2, false, kDevArgs><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
+    }
+  }
+  return check_launch("subs_sample_kernel launch");
+}
+}  // namespace
+}  // extern "C++"
+
+int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B, int64_t S,
+                    int64_t V, const int64_t* xt, int64_t mask_index, double t, double s,
+                    uint64_t seed, uint64_t offset, const double* uniforms, int64_t* out,
+                    int dtype, void* stream) {
+  if (const int rc = check_sample_args(logits, B, S, V, xt, mask_index, out, dtype);
+      rc != BD3_OK)
+    return rc;
   if (!(t > 0.0)) return fail(BD3_ERR_INVALID, "t must be > 0 (the step divides by it)");
   if (const int rc = ensure_context(); rc != BD3_OK) return rc;
   bd3::SampleParams p{};
@@ -852,25 +887,34 @@ int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B,
   p.B = static_cast<int>(B);
   p.S = static_cast<int>(S);
   p.V = static_cast<int>(V);
-  const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const unsigned blocks = static_cast<unsigned>(B * S);
-  {
-    ProfScope ps(kPfSample, st);
-    // bf16 rows up to 100,000 entries are staged in shared memory (two CTAs per SM)
-    constexpr size_t kMaxStage = 200016;
-    const size_t stage = static_cast<size_t>(V) * 2 + 16;
-    if (dtype == BD3_BF16 && stage <= kMaxStage) {
-      auto kern = bd3::subs_sample_kernel<0, true>;
-      if (const int rc = set_smem(kern, static_cast<uint32_t>(kMaxStage), 16); rc != BD3_OK)
-        return rc;
-      kern<<<blocks, bd3::kSampleThreads, stage, st>>>(p);
-    } else if (dtype == BD3_BF16) {
-      bd3::subs_sample_kernel<0, false><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
-    } else {
-      bd3::subs_sample_kernel<2, false><<<blocks, bd3::kSampleThreads, 0, st>>>(p);
-    }
-  }
-  return check_launch("subs_sample_kernel launch");
+  return launch_sample<false>(p, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// The same step with (t, s) and (seed, offset) in device memory (the Philox draw only), so
+// that a sampling loop captured in a CUDA graph advances them on the device between replays.
+int bd3_subs_sample_dev(const void* logits, const int64_t* logit_strides, int64_t B,
+                        int64_t S, int64_t V, const int64_t* xt, int64_t mask_index,
+                        const double* ts, const uint64_t* seed_offset, int64_t* out, int dtype,
+                        void* stream) {
+  if (const int rc = check_sample_args(logits, B, S, V, xt, mask_index, out, dtype);
+      rc != BD3_OK)
+    return rc;
+  if (ts == nullptr || seed_offset == nullptr)
+    return fail(BD3_ERR_INVALID, "ts (t, s) and seed_offset (seed, offset) are required");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  bd3::SampleParams p{};
+  p.logits = logits;
+  p.l_sb = logit_strides[0];
+  p.l_ss = logit_strides[1];
+  p.xt = reinterpret_cast<const long long*>(xt);
+  p.out = reinterpret_cast<long long*>(out);
+  p.ts_dev = ts;
+  p.rng_dev = reinterpret_cast<const unsigned long long*>(seed_offset);
+  p.mask_index = mask_index;
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.V = static_cast<int>(V);
+  return launch_sample<true>(p, dtype, static_cast<cudaStream_t>(stream));
 }
 
 int bd3_profile_enable(int on) {

@@ -44,6 +44,8 @@ struct SampleParams {
   double keep;               // 1 - s/t, the weight of the unmasking tokens
   double stay;               // s/t, the weight of staying masked
   long long mask_index;
+  const double* ts_dev;                  // optional device (t, s): overrides keep and stay
+  const unsigned long long* rng_dev;     // optional device (seed, offset): overrides both
   int B, S, V;
 };
 
@@ -110,7 +112,13 @@ __device__ __forceinline__ void best_of(double& s, int& i, double s2, int i2) {
 // kStage: the row is first copied into shared memory with 16-byte loads (a scalar head up to
 // the first 16-byte boundary, then whole pieces, then a scalar tail), and the three passes
 // read it from there; the element order of every pass is the same either way.
-template <int kDtype, bool kStage>
+//
+// kDevArgs: the step's (t, s) and (seed, offset) are read from ts_dev and rng_dev on the
+// device, so the launch arguments stay fixed from step to step and a CUDA graph captured
+// once draws each step afresh. The weights are computed as on the host (1 - s/t and s/t in
+// float64, IEEE division), so they equal the host-argument launch's bit for bit. A device
+// t <= 0 (or NaN) raises status bit 2 and leaves every token as it was.
+template <int kDtype, bool kStage, bool kDevArgs>
 __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const SampleParams p) {
   extern __shared__ __align__(16) uint16_t srow_raw[];
   __shared__ float red[kSampleThreads / 32];
@@ -121,8 +129,13 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   const int row = blockIdx.x;
   const int b = row / p.S, i = row % p.S;
   const long long tok = p.xt[static_cast<long long>(b) * p.S + i];
-  if (tok != p.mask_index) {  // carry-over: the reference's where() keeps the token
-    if (threadIdx.x == 0) p.out[static_cast<long long>(b) * p.S + i] = tok;
+  bool bad_ts = false;
+  if constexpr (kDevArgs) bad_ts = !(p.ts_dev[0] > 0.0);
+  if (tok != p.mask_index || bad_ts) {  // carry-over: the reference's where() keeps the token
+    if (threadIdx.x == 0) {
+      p.out[static_cast<long long>(b) * p.S + i] = tok;
+      if (bad_ts && row == 0) atomicOr(&g_bd3_status, kStatusBadLaunch);
+    }
     return;
   }
   const void* lrow = reinterpret_cast<const uint8_t*>(p.logits) +
@@ -198,10 +211,16 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   const float lse = rnd<kDtype>(logf(sum));
   // pass 2: q_j in float64 (the reference's exp(log_probs).double() * (1 - s/t), s/t at
   // mask_index), then one draw.
+  double keep = p.keep, stay = p.stay;
+  if constexpr (kDevArgs) {
+    const double t = p.ts_dev[0], s = p.ts_dev[1];
+    keep = 1.0 - s / t;
+    stay = s / t;
+  }
   auto q64 = [&](int j) -> double {
-    if (j == mask) return p.stay;
+    if (j == mask) return stay;
     const float lp = rnd<kDtype>(rnd<kDtype>(logit(j) - mx) - lse);
-    return static_cast<double>(rnd<kDtype>(expf(lp))) * p.keep;
+    return static_cast<double>(rnd<kDtype>(expf(lp))) * keep;
   };
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   long long pick;
@@ -269,9 +288,11 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     double excl = __shfl_up_sync(0xffffffffu, incl, 1);
     if (l == 0) excl = w > 0 ? last_incl[w - 1] : 0.0;
     const double total = last_incl[kSampleThreads / 32 - 1];
-    const U4 r = philox4x32_10(U4{static_cast<uint32_t>(row), static_cast<uint32_t>(p.offset),
-                                  static_cast<uint32_t>(p.offset >> 32), 0x5A3u},
-                               static_cast<uint32_t>(p.seed), static_cast<uint32_t>(p.seed >> 32));
+    unsigned long long seed = p.seed, offset = p.offset;
+    if constexpr (kDevArgs) seed = p.rng_dev[0], offset = p.rng_dev[1];
+    const U4 r = philox4x32_10(U4{static_cast<uint32_t>(row), static_cast<uint32_t>(offset),
+                                  static_cast<uint32_t>(offset >> 32), 0x5A3u},
+                               static_cast<uint32_t>(seed), static_cast<uint32_t>(seed >> 32));
     double target = u53(r.x, r.y) * total;
     if (target >= total) target = nextafter(total, 0.0);
     int mine = 0x7fffffff;

@@ -195,13 +195,26 @@ BD3_API int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int6
  *           op to that dtype, as the reference's tensors of that dtype do.
  *   xt: device int64 (B, S) tokens; out: device int64 (B, S) next tokens (may alias xt).
  *   t, s: the step's times (t > 0). Tokens that are not mask_index are kept.
- *   uniforms: NULL to draw u with Philox4x32-10 keyed by `seed` (counter: pair index, row,
- *   offset), or a device float64 (B, S, V) contiguous tensor of uniforms in [0, 1) to
- *   replay a given draw (the reference's torch.rand_like). */
+ *   uniforms: NULL for the production draw, an exact draw from q / sum(q) by inverse CDF
+ *   with one Philox4x32-10 uniform per row (key = seed, counter = (row, offset low 32 bits,
+ *   offset high 32 bits, 0x5A3)), or a device float64 (B, S, V) contiguous tensor of
+ *   uniforms in [0, 1) to replay the reference's Gumbel-max on a given draw (its
+ *   torch.rand_like). */
 BD3_API int bd3_subs_sample(const void* logits, const int64_t* logit_strides, int64_t B,
                             int64_t S, int64_t V, const int64_t* xt, int64_t mask_index,
                             double t, double s, uint64_t seed, uint64_t offset,
                             const double* uniforms, int64_t* out, int dtype, void* stream);
+
+/* bd3_subs_sample's production draw with its per-step values in device memory:
+ * ts = device float64 (t, s), seed_offset = device uint64 (seed, offset). The launch then
+ * does not change from step to step, so a sampling loop captured once in a CUDA graph
+ * draws every step afresh once the caller advances them on the device. Same tokens as
+ * bd3_subs_sample with those values as host arguments (same sampler.py:100-122 step).
+ * A device t <= 0 keeps every token and sets device status bit 2. */
+BD3_API int bd3_subs_sample_dev(const void* logits, const int64_t* logit_strides, int64_t B,
+                                int64_t S, int64_t V, const int64_t* xt, int64_t mask_index,
+                                const double* ts, const uint64_t* seed_offset, int64_t* out,
+                                int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Per-kernel timing for benchmarks. While enabled, every launch is bracketed by a pair of

@@ -103,3 +103,18 @@ def test_capi_sampler_argument_checks():
     assert _call(t=0.0) == BD3_ERR_INVALID
     assert _call(V=1, mask=0) == BD3_ERR_INVALID
     assert _call(xt=None) == BD3_ERR_INVALID
+
+
+def test_capi_sampler_device_args_checks():
+    """bd3_subs_sample_dev: the same argument checks, and both device value pointers
+    required (rejected before any CUDA call)."""
+    from bd3attn._lib import BD3_ERR_INVALID, LIB, i64_array
+
+    def call(ts=0x5000, rng=0x6000, dtype=2, mask=99):
+        return LIB.bd3_subs_sample_dev(0x1000, i64_array((400, 100)), 2, 4, 100, 0x2000, mask,
+                                       ts, rng, 0x3000, dtype, None)
+    assert call(ts=None) == BD3_ERR_INVALID
+    assert "ts (t, s)" in LIB.bd3_last_error().decode()
+    assert call(rng=None) == BD3_ERR_INVALID
+    assert call(dtype=1) == BD3_ERR_INVALID
+    assert call(mask=100) == BD3_ERR_INVALID
