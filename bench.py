@@ -465,6 +465,40 @@ def graph_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """Training tokens/s of the stand-in BD3-LM backbone at the reference's training config
+    (train/train.py:30-60: d_model 768, 12 layers of 12 heads, d_ff 3072, seq_len 1024 so the
+    DiT sees 2n = 2048, block_size 16, batch 16, vocabulary 50258, bf16 autocast, AdamW with
+    gradient clipping), once with the "bsfa" backend (the sm_100a kernels) and once with
+    "sdpa" (PyTorch's attention given the boolean mask), from the same weights and batches.
+    tokens/s = batch * seq_len / median step time, the reference's formula (:294)."""
+    import copy
+
+    from bench import attention as ba
+    from bench import backbone as bb
+    Bt, n, bs, V = 16, 1024, 16, 50258
+    torch.manual_seed(0)
+    base = bb.Backbone(V, n, bs).to(dev)
+    gen = torch.Generator().manual_seed(3)
+    batches = [tuple(t.to(dev) for t in bb.noisy_batch(gen, Bt, n, bs, V)) for _ in range(4)]
+    out = {}
+    for name in ("bsfa", "sdpa"):
+        model = copy.deepcopy(base)
+        ba.install_attention(name, block_size=bs, modules=bb.ATTENTION)
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.999),
+                                weight_decay=0.0)
+        for i in range(3):
+            bb.train_step(model, opt, *batches[i % 4])
+        it = iter(range(10 ** 9))
+        ms = time_steps(lambda: bb.train_step(model, opt, *batches[next(it) % 4]), reps, l2)
+        t = statistics.median(ms)
+        out[name] = {"ms_per_step": round(t, 2), "tokens_per_s": round(Bt * n / (t * 1e-3))}
+        del model, opt
+        torch.cuda.empty_cache()
+    out["speedup"] = round(out["sdpa"]["ms_per_step"] / out["bsfa"]["ms_per_step"], 3)
+    return {"train_step_b16_n1024": out}
+
+
 def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
     """One denoising step of the block sampler at the generation config:
     B=64 sequences, a 16-token block, vocabulary 50258, bf16 logits (the backbone runs under
@@ -715,7 +749,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
-    ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step"),
+    ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step",
+                                        "train_step"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -727,7 +762,8 @@ def main():
         dev = torch.device("cuda", 0)
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
         fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
-              "live_decode": live_decode_extras, "graph_step": graph_step_extras}[args.extra]
+              "live_decode": live_decode_extras, "graph_step": graph_step_extras,
+              "train_step": train_step_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)
