@@ -17,9 +17,10 @@
 // tensor (the reference's torch.rand_like), g_j = EPS - log(u_j + EPS), token = argmax_j
 // q_j / g_j (the first index among equal maxima, as torch.argmax); or, in production, an
 // exact draw from the same distribution q / sum(q) by inverse CDF with one uniform per row:
-// the elements are ordered (thread t, then j = t, t + T, t + 2T, ...), each thread sums its
-// q_j in float64 in that order, a block scan (Hillis-Steele within warps, then over the
-// warp totals) gives every thread its slice [excl, incl) of [0, total), and
+// the elements are ordered (thread t, then its chunks c = t, t + T, t + 2T, ..., each the 8
+// entries [8c, 8c + 8) in order), each thread sums its q_j in float64 in that order, a block
+// scan (Hillis-Steele within warps, then over the warp totals) gives every thread its slice
+// [excl, incl) of [0, total), and
 // r * total with r = (x << 21 | y >> 11) * 2^-53 from words x, y of Philox4x32-10 (Salmon,
 // Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3", SC 2011) at counter
 // (row, offset lo, offset hi, 0x5A3) under key = seed falls in one slice, whose thread walks
@@ -104,14 +105,92 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return __shfl_sync(0xffffffffu, v, 0);
 }
 
+constexpr int kChunk = 8;               // entries of a 16-byte chunk of a bf16 row
+constexpr uint16_t kBf16NegInf = 0xFF80u;
+
+__device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) {
+  return *reinterpret_cast<const __nv_bfloat162*>(&u);
+}
+
+// Round a pair to the dtype with one packed conversion (bf16 and fp16; fp32 is left as is).
+template <int kDtype>
+__device__ __forceinline__ void rnd2(float& a, float& b) {
+  if constexpr (kDtype == 0) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+    a = __low2float(v), b = __high2float(v);
+  } else if constexpr (kDtype == 1) {
+    const __half2 v = __floats2half2_rn(a, b);
+    a = __low2float(v), b = __high2float(v);
+  }
+}
+
+// Bytes [a, a + 16) of the 32 bytes lo:hi (a even, q = a / 4 words and r = 8 * (a % 4) bits).
+template <int kQ>
+__device__ __forceinline__ uint4 realign_q(const uint32_t (&w)[8], int r) {
+  return make_uint4(__funnelshift_r(w[kQ], w[kQ + 1], r), __funnelshift_r(w[kQ + 1], w[kQ + 2], r),
+                    __funnelshift_r(w[kQ + 2], w[kQ + 3], r),
+                    __funnelshift_r(w[kQ + 3], w[kQ + 4], r));
+}
+__device__ __forceinline__ uint4 realign(uint4 lo, uint4 hi, int a) {
+  const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+  const int r = (a & 3) * 8;
+  switch (a >> 2) {  // uniform over the CTA (one row)
+    case 0: return realign_q<0>(w, r);
+    case 1: return realign_q<1>(w, r);
+    case 2: return realign_q<2>(w, r);
+    default: return realign_q<3>(w, r);
+  }
+}
+
+// Copy a 16-bit row of V entries into shared memory so that entry j sits at dst16[j] with
+// dst 16-byte aligned, whatever the row's own alignment: 16-byte loads of the aligned words
+// that hold the row's bytes (lane m of a warp loads word c and takes word c + 1 from lane
+// m + 1), realigned in registers. Chunk c of dst (entries [8c, 8c + 8)) is written for
+// c < n_chunks; entries past V are left for the caller to overwrite. Only words that hold at
+// least one byte of the row are read.
+__device__ __forceinline__ void stage_row(const uint16_t* g16, int V, int n_chunks, uint4* dst) {
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(g16);
+  const int a = static_cast<int>(addr & 15u);
+  const uint4* src = reinterpret_cast<const uint4*>(addr - static_cast<uintptr_t>(a));
+  const int n_words = (a + 2 * V + 15) >> 4;
+  const int lane = threadIdx.x & 31;
+  constexpr int kDepth = 4;  // chunks in flight per thread
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int c0 = static_cast<int>(threadIdx.x & ~31u); c0 < n_chunks;
+       c0 += kDepth * kSampleThreads) {
+    uint4 lo[kDepth], edge[kDepth];
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) {
+      const int c = c0 + d * kSampleThreads + lane;
+      lo[d] = c < n_words ? src[c] : zero;
+      edge[d] = (lane == 31 && c + 1 < n_words) ? src[c + 1] : zero;
+    }
+#pragma unroll
+    for (int d = 0; d < kDepth; ++d) {
+      const int c = c0 + d * kSampleThreads + lane;
+      uint4 hi;
+      hi.x = __shfl_down_sync(0xffffffffu, lo[d].x, 1);
+      hi.y = __shfl_down_sync(0xffffffffu, lo[d].y, 1);
+      hi.z = __shfl_down_sync(0xffffffffu, lo[d].z, 1);
+      hi.w = __shfl_down_sync(0xffffffffu, lo[d].w, 1);
+      if (lane == 31) hi = edge[d];
+      if (c < n_chunks) dst[c] = realign(lo[d], hi, a);
+    }
+  }
+}
+
 // (score, index) with the larger score, the smaller index on a tie (torch.argmax's first max).
 __device__ __forceinline__ void best_of(double& s, int& i, double s2, int i2) {
   if (s2 > s || (s2 == s && i2 < i)) s = s2, i = i2;
 }
 
-// kStage: the row is first copied into shared memory with 16-byte loads (a scalar head up to
-// the first 16-byte boundary, then whole pieces, then a scalar tail), and the three passes
-// read it from there; the element order of every pass is the same either way.
+// The row is processed in chunks of 8 consecutive entries, thread t taking chunks t, t + T,
+// t + 2T, ... (T = 512) in every pass. kStage (bf16 rows): the row is first copied into
+// shared memory, realigned so that each chunk is one 16-byte word, with the [MASK] entry
+// biased and the last chunk padded with -inf, so the passes read a chunk with one 16-byte
+// load and need no bounds or [MASK] test; the max is taken on packed bf16 pairs. Without
+// staging (fp32 rows, or bf16 rows too long for shared memory) each chunk's entries are
+// read from global memory. The element order, and so the draw, is the same either way.
 //
 // kDevArgs: the step's (t, s) and (seed, offset) are read from ts_dev and rng_dev on the
 // device, so the launch arguments stay fixed from step to step and a CUDA graph captured
@@ -140,76 +219,79 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   }
   const void* lrow = reinterpret_cast<const uint8_t*>(p.logits) +
                      (b * p.l_sb + i * p.l_ss) * (kDtype == 2 ? 4 : 2);
-  // staged rows: element j at srow_raw[j + shift], shift making the global 16-byte pieces
-  // land on 16-byte shared-memory boundaries
-  int shift = 0;
-  if constexpr (kStage) {
-    static_assert(kDtype != 2, "staging holds 16-bit rows");
-    const uint16_t* g16 = reinterpret_cast<const uint16_t*>(lrow);
-    const int head = min(p.V, static_cast<int>(((16u - (reinterpret_cast<uintptr_t>(g16) & 15u)) & 15u) >> 1));
-    shift = (8 - head) & 7;
-    const int body = (p.V - head) >> 3;  // whole 16-byte pieces after the head
-    if (threadIdx.x < head) srow_raw[threadIdx.x + shift] = g16[threadIdx.x];
-    const uint4* src = reinterpret_cast<const uint4*>(g16 + head);
-    uint4* dst = reinterpret_cast<uint4*>(srow_raw + head + shift);
-    for (int c = threadIdx.x; c < body; c += 4 * kSampleThreads) {
-      uint4 v[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (c + k * kSampleThreads < body) v[k] = src[c + k * kSampleThreads];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (c + k * kSampleThreads < body) dst[c + k * kSampleThreads] = v[k];
-    }
-    for (int j = head + 8 * body + threadIdx.x; j < p.V; j += kSampleThreads)
-      srow_raw[j + shift] = g16[j];
-    __syncthreads();
-  }
-  auto logit = [&](int j) -> float {
-    if constexpr (kStage) {
-      const uint16_t h = srow_raw[j + shift];
-      if constexpr (kDtype == 0) return __uint_as_float(static_cast<uint32_t>(h) << 16);
-      else return __half2float(__ushort_as_half(h));
-    } else {
-      return logit_at<kDtype>(lrow, j);
-    }
-  };
   const int mask = static_cast<int>(p.mask_index);
   const float bias = rnd<kDtype>(-1e6f);  // model/subs.py:8
-  // pass 1: max and sum of exp(x - max) of the biased logits; kUnroll independent loads in
-  // flight per thread
-  constexpr int kUnroll = 8;
-  auto biased = [&](int j) {
-    const float x = logit(j);
-    return j == mask ? rnd<kDtype>(x + bias) : x;
-  };
-  float mx = -INFINITY;
-  for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
-    float x[kUnroll];
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
-      const int jj = j + k * kSampleThreads;
-      x[k] = jj < p.V ? biased(jj) : -INFINITY;
+  const int n_chunks = (p.V + kChunk - 1) / kChunk;
+  // staged rows: element j at srow[j] (16-byte aligned whatever the row's alignment), the
+  // [MASK] entry already biased, and the last chunk padded with -inf
+  uint4* const schunk = reinterpret_cast<uint4*>(srow_raw);
+  if constexpr (kStage) {
+    static_assert(kDtype == 0, "staging holds bf16 rows");
+    stage_row(reinterpret_cast<const uint16_t*>(lrow), p.V, n_chunks, schunk);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const float x = __uint_as_float(static_cast<uint32_t>(srow_raw[mask]) << 16);
+      srow_raw[mask] = static_cast<uint16_t>(__float_as_uint(rnd<kDtype>(x + bias)) >> 16);
     }
+    if (threadIdx.x < kChunk * n_chunks - p.V) srow_raw[p.V + threadIdx.x] = kBf16NegInf;
+    __syncthreads();
+  }
+  // the 8 (biased) logits of chunk c, -inf past the vocabulary
+  auto chunk = [&](int c, float (&x)[kChunk]) {
+    if constexpr (kStage) {
+      const uint4 v = schunk[c];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) mx = fmaxf(mx, x[k]);
+      for (int k = 0; k < 4; ++k) {
+        x[2 * k] = __uint_as_float(w[k] << 16);
+        x[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k) {
+        const int j = c * kChunk + k;
+        const float v = j < p.V ? logit_at<kDtype>(lrow, j) : -INFINITY;
+        x[k] = j == mask ? rnd<kDtype>(v + bias) : v;
+      }
+    }
+  };
+  // pass 1: the row max
+  float mx = -INFINITY;
+  if constexpr (kStage) {  // bf16 max is exact: compare packed pairs
+    __nv_bfloat162 m2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);
+    for (int c = threadIdx.x; c < n_chunks; c += kSampleThreads) {
+      const uint4 v = schunk[c];
+      m2 = __hmax2(m2, __hmax2(__hmax2(as_bf162(v.x), as_bf162(v.y)),
+                               __hmax2(as_bf162(v.z), as_bf162(v.w))));
+    }
+    mx = fmaxf(__low2float(m2), __high2float(m2));
+  } else {
+    for (int c = threadIdx.x; c < n_chunks; c += kSampleThreads) {
+      float x[kChunk];
+      chunk(c, x);
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k) mx = fmaxf(mx, x[k]);
+    }
   }
   mx = block_max(mx, red);
+  // pass 2: sum of exp(x - max), each op rounded to the dtype
   float sum = 0.f;
-  for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
-    float x[kUnroll];
+  for (int c = threadIdx.x; c < n_chunks; c += kSampleThreads) {
+    float x[kChunk];
+    chunk(c, x);
 #pragma unroll
-    for (int k = 0; k < kUnroll; ++k) {
-      const int jj = j + k * kSampleThreads;
-      x[k] = jj < p.V ? biased(jj) : -INFINITY;
+    for (int k = 0; k < kChunk; k += 2) {
+      float a = x[k] - mx, bb = x[k + 1] - mx;
+      rnd2<kDtype>(a, bb);
+      a = expf(a), bb = expf(bb);
+      rnd2<kDtype>(a, bb);
+      sum += a;
+      sum += bb;
     }
-#pragma unroll
-    for (int k = 0; k < kUnroll; ++k)
-      if (j + k * kSampleThreads < p.V) sum += rnd<kDtype>(expf(rnd<kDtype>(x[k] - mx)));
   }
   sum = rnd<kDtype>(block_sum(sum, red));
   const float lse = rnd<kDtype>(logf(sum));
-  // pass 2: q_j in float64 (the reference's exp(log_probs).double() * (1 - s/t), s/t at
+  // pass 3: q_j in float64 (the reference's exp(log_probs).double() * (1 - s/t), s/t at
   // mask_index), then one draw.
   double keep = p.keep, stay = p.stay;
   if constexpr (kDevArgs) {
@@ -217,9 +299,33 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     keep = 1.0 - s / t;
     stay = s / t;
   }
+  // q of the 8 entries of chunk c (0 past the vocabulary)
+  auto chunk_q = [&](int c, double (&q)[kChunk]) {
+    float x[kChunk];
+    chunk(c, x);
+#pragma unroll
+    for (int k = 0; k < kChunk; k += 2) {
+      float a = x[k] - mx, bb = x[k + 1] - mx;
+      rnd2<kDtype>(a, bb);
+      a -= lse, bb -= lse;
+      rnd2<kDtype>(a, bb);
+      a = expf(a), bb = expf(bb);
+      rnd2<kDtype>(a, bb);
+      q[k] = static_cast<double>(a) * keep;
+      q[k + 1] = static_cast<double>(bb) * keep;
+    }
+    if (c == mask / kChunk) {
+#pragma unroll
+      for (int k = 0; k < kChunk; ++k)
+        if (c * kChunk + k == mask) q[k] = stay;
+    }
+  };
   auto q64 = [&](int j) -> double {
     if (j == mask) return stay;
-    const float lp = rnd<kDtype>(rnd<kDtype>(logit(j) - mx) - lse);
+    float x;
+    if constexpr (kStage) x = __uint_as_float(static_cast<uint32_t>(srow_raw[j]) << 16);
+    else x = logit_at<kDtype>(lrow, j);
+    const float lp = rnd<kDtype>(rnd<kDtype>(x - mx) - lse);
     return static_cast<double>(rnd<kDtype>(expf(lp))) * keep;
   };
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -249,19 +355,16 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     }
     pick = best_i;
   } else {
-    // inverse CDF over the element order (thread t, then j = t, t + T, t + 2T, ...): each
-    // thread sums its q_j in that order, a block scan gives each thread its slice
-    // [excl_t, incl_t) of [0, total), and one Philox uniform r per row selects r * total.
+    // inverse CDF over the element order (thread t, its chunks c = t, t + T, t + 2T, ...,
+    // the 8 entries of each chunk in order): each thread sums its q_j in that order, a
+    // block scan gives each thread its slice [excl_t, incl_t) of [0, total), and one Philox
+    // uniform r per row selects r * total.
     double part = 0.0;
-    for (int j = threadIdx.x; j < p.V; j += kUnroll * kSampleThreads) {
-      double q[kUnroll];
+    for (int c = threadIdx.x; c < n_chunks; c += kSampleThreads) {
+      double q[kChunk];
+      chunk_q(c, q);
 #pragma unroll
-      for (int k = 0; k < kUnroll; ++k) {
-        const int jj = j + k * kSampleThreads;
-        q[k] = jj < p.V ? q64(jj) : 0.0;
-      }
-#pragma unroll
-      for (int k = 0; k < kUnroll; ++k) part += q[k];
+      for (int k = 0; k < kChunk; ++k) part += q[k];
     }
     // inclusive scan: within warps (Hillis-Steele), then of the warp totals in warp 0
     double x = part;
@@ -296,24 +399,19 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     double target = u53(r.x, r.y) * total;
     if (target >= total) target = nextafter(total, 0.0);
     int mine = 0x7fffffff;
-    if (excl <= target && target < incl) {  // this thread's slice: walk it, kUnroll weights
-      const double local = target - excl;  // loaded at a time, added in the same order as part
+    if (excl <= target && target < incl) {  // this thread's slice: walk it chunk by chunk,
+      const double local = target - excl;  // adding in the same order as part
       double acc = 0.0;
       int last_nz = 0x7fffffff;
-      for (int j = threadIdx.x; j < p.V && mine == 0x7fffffff; j += kUnroll * kSampleThreads) {
-        double q[kUnroll];
+      for (int c = threadIdx.x; c < n_chunks && mine == 0x7fffffff; c += kSampleThreads) {
+        double q[kChunk];
+        chunk_q(c, q);
 #pragma unroll
-        for (int k = 0; k < kUnroll; ++k) {
-          const int jj = j + k * kSampleThreads;
-          q[k] = jj < p.V ? q64(jj) : 0.0;
-        }
-#pragma unroll
-        for (int k = 0; k < kUnroll; ++k) {
-          const int jj = j + k * kSampleThreads;
-          if (mine != 0x7fffffff || jj >= p.V) continue;
+        for (int k = 0; k < kChunk; ++k) {
+          if (mine != 0x7fffffff) continue;
           acc += q[k];
-          if (q[k] > 0.0) last_nz = jj;
-          if (local < acc) mine = jj;
+          if (q[k] > 0.0) last_nz = c * kChunk + k;
+          if (local < acc) mine = c * kChunk + k;
         }
       }
       if (mine == 0x7fffffff) mine = last_nz;  // the local offset rounded past the slice

@@ -8,7 +8,8 @@ Reference files restated here (paths inside tusharsonthalia/diffusion-llm):
   sample/sampler.py:8-34     sample_categorical: argmax(probs / (EPS - log(u + EPS)))
   sample/sampler.py:100-122  q = exp(log_probs).double() * (1 - s/t), q[mask] = s/t, where()
 and the kernel's own draw: Philox4x32-10 (Salmon et al., SC 2011) row uniforms and its
-inverse CDF over (thread, stride) order with a Hillis-Steele block scan.
+inverse CDF over the kernel's element order (thread t, its 8-entry chunks t, t + 512, ...)
+with a Hillis-Steele block scan.
 """
 
 from __future__ import annotations
@@ -62,15 +63,23 @@ def _hillis_steele(x: list) -> list:
     return x
 
 
+def thread_order(V: int, t: int, threads: int = 512, chunk: int = 8) -> list[int]:
+    """The entries thread t of the kernel takes, in its order: chunks c = t, t + threads,
+    ..., each the `chunk` consecutive entries [chunk * c, chunk * c + chunk) below V."""
+    n_chunks = (V + chunk - 1) // chunk
+    return [j for c in range(t, n_chunks, threads) for j in range(chunk * c, min(chunk * c + chunk, V))]
+
+
 def inverse_cdf(q: np.ndarray, r: float, threads: int = 512):
     """The kernel's inverse-CDF draw from one row of weights q (V,) float64 and a uniform r:
     (index, margin) where margin is the distance of r * total to the nearest slice or
     element boundary, relative to total (rounding decides draws closer than ~1e-15)."""
     V = q.shape[0]
+    orders = [thread_order(V, t, threads) for t in range(threads)]
     part = [np.float64(0.0)] * threads
     for t in range(threads):
         acc = np.float64(0.0)
-        for j in range(t, V, threads):
+        for j in orders[t]:
             acc = acc + q[j]
         part[t] = acc
     warps = threads // 32
@@ -89,7 +98,7 @@ def inverse_cdf(q: np.ndarray, r: float, threads: int = 512):
         if excl[t] <= target < incl[t]:
             local = target - excl[t]
             acc, last_nz, mine = np.float64(0.0), None, None
-            for j in range(t, V, threads):
+            for j in orders[t]:
                 acc = acc + q[j]
                 bounds.append(excl[t] + acc)
                 if q[j] > 0:

@@ -46,7 +46,9 @@ def test_replayed_uniforms_reproduce_reference_tokens(gs, tag, dt):
 
 
 @pytest.mark.parametrize("dt,V,B,S", [("bf16", 50258, 2, 16), ("f32", 50258, 1, 16),
-                                      ("f32", 1001, 3, 5)])
+                                      ("f32", 1001, 3, 5),
+                                      ("bf16", 1001, 3, 5),   # rows at every 2-byte offset
+                                      ("bf16", 9, 2, 4)])     # two chunks, one entry in the last
 def test_philox_draw_equals_oracle(dt, V, B, S):
     """The production draw (inverse CDF, one Philox uniform per row) equals the oracle's
     replay of the same arithmetic wherever rounding cannot decide it."""
@@ -86,12 +88,13 @@ def test_draws_follow_the_step_distribution():
     assert chi2 < 30.0, (chi2, counts, rows * p)  # P(chi2_7 > 30) < 1e-4
 
 
-def test_strided_logits_and_in_place_update():
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_strided_logits_and_in_place_update(dt):
     """Logits as a slice of the backbone's (batch, seq, vocab) output, and out aliasing xt."""
     from bd3attn.sampler import subs_sample_step
     g = torch.Generator().manual_seed(8)
     V, mask = 777, 776
-    full = torch.randn(2, 20, V, generator=g).cuda()
+    full = torch.randn(2, 20, V, generator=g).to(dt).cuda()
     logits = full[:, -16:]  # model/bd3lm.py:164 takes the block's last positions
     xt = torch.randint(0, V - 1, (2, 16), generator=g)
     xt[:, ::2] = mask

@@ -40,11 +40,14 @@ def test_row_uniforms_in_range_and_distinct():
 
 def test_inverse_cdf_scan_and_walk():
     """The kernel's slice arithmetic: every target falls in the element whose cumulative
-    range (in the (thread, stride) order) holds it, including zero-weight elements."""
+    range (in the kernel's order: thread t, its 8-entry chunks t, t + 512, ...) holds it,
+    including zero-weight elements."""
     rng = np.random.default_rng(0)
-    q = rng.random(2000)
-    q[rng.random(2000) < 0.3] = 0.0
-    order = [j for t in range(512) for j in range(t, 2000, 512)]
+    q = rng.random(5003)
+    q[rng.random(5003) < 0.3] = 0.0
+    order = [j for t in range(512) for j in osm.thread_order(5003, t)]
+    assert sorted(order) == list(range(5003))
+    assert order[:10] == [0, 1, 2, 3, 4, 5, 6, 7, 4096, 4097]
     cum = np.cumsum(q[order])
     for r in (0.0, 1e-9, 0.25, 0.5, 0.999999, 1 - 2 ** -53):
         j, margin = osm.inverse_cdf(q, r)
