@@ -499,6 +499,49 @@ def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     return {"train_step_b16_n1024": out}
 
 
+def generation_extras(dev, l2, peaks, reps: int = 10, world: int = 1, rank: int = 0) -> dict:
+    """Benchmark config 5 with the stand-in backbone (12 layers, d_model 768, 12 heads, d_ff
+    3072, vocabulary 50258, bf16 weights, random init): 64 sequences generated to 1024 tokens
+    in 16-token blocks, 16 sampler steps per block, through bench/generation.py's
+    CachedGeneration (in-place cache, split-KV decode, fused sampler, one CUDA graph replay
+    per block) and, on one GPU, ReferenceGeneration (the reference's flow in eager PyTorch
+    ops). Under torchrun the batch is split over the ranks (64 / world sequences each, no
+    communication) and the time is the max over ranks, so tokens/s is the whole job's.
+    tokens/s = 64 * 1024 / time (CUDA events; ours is timed after a run that captures its
+    graph)."""
+    from bench.backbone import Backbone
+    from bench.generation import CachedGeneration, ReferenceGeneration
+    Bg, n_blocks, steps, V = 64, 64, 16, 50258
+    b_local = Bg // world
+    torch.manual_seed(0)  # the same weights on every rank
+    model = Backbone(V, 1024, BS).to(dev).bfloat16().eval()
+
+    def timed(fn) -> float:
+        flush_l2(l2)
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(a.elapsed_time(b), world)
+
+    ours = CachedGeneration(model, b_local, n_blocks, steps, seed=1 + rank)
+    ours.run()
+    t_ours = statistics.median([timed(ours.run) for _ in range(2)])
+    toks = Bg * n_blocks * BS
+    out = {"gpus": world, "sequences_per_gpu": b_local,
+           "ours": {"ms": round(t_ours, 1), "tokens_per_s": round(toks / (t_ours * 1e-3))}}
+    if world == 1:
+        ReferenceGeneration(model, Bg, 1, steps).run()  # warm-up (library set-up)
+        t_ref = timed(ReferenceGeneration(model, Bg, n_blocks, steps,
+                                          generator=torch.Generator(device=dev).manual_seed(1)).run)
+        out["reference_flow"] = {"ms": round(t_ref, 1),
+                                 "tokens_per_s": round(toks / (t_ref * 1e-3))}
+        out["speedup"] = round(t_ref / t_ours, 2)
+    return {"generation_b64_l1024": out}
+
+
 def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
     """One denoising step of the block sampler at the generation config:
     B=64 sequences, a 16-token block, vocabulary 50258, bf16 logits (the backbone runs under
@@ -750,20 +793,30 @@ def main():
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
     ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step",
-                                        "train_step"),
+                                        "train_step", "generation"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.decode_only:
         run_decode_only(args)
+    elif args.extra == "generation":
+        world, rank, local = dist_setup(args.gpus)
+        dev = torch.device("cuda", local)
+        l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+        res = generation_extras(dev, l2, load_peaks(), world=world, rank=rank)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
     elif args.extra:
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
         fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
               "live_decode": live_decode_extras, "graph_step": graph_step_extras,
-              "train_step": train_step_extras}[args.extra]
+              "train_step": train_step_extras, "generation": generation_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)

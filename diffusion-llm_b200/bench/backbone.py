@@ -80,7 +80,8 @@ class Backbone(nn.Module):
     def __init__(self, vocab_size: int, n: int, block_size: int, d_model: int = 768,
                  n_heads: int = 12, n_layers: int = 12, d_ff: int = 3072):
         super().__init__()
-        self.n, self.mask_index = n, vocab_size - 1
+        self.n, self.mask_index, self.block_size = n, vocab_size - 1, block_size
+        self.n_heads = n_heads
         self.embed = nn.Embedding(vocab_size, d_model)
         self.layers = nn.ModuleList(Layer(d_model, n_heads, d_ff) for _ in range(n_layers))
         self.norm = nn.LayerNorm(d_model)
@@ -91,11 +92,18 @@ class Backbone(nn.Module):
         self.register_buffer("sin", sin[pos], persistent=False)
         self.register_buffer("attn_mask", block_diff_mask(n, block_size), persistent=False)
 
-    def forward(self, xt: torch.Tensor, x0: torch.Tensor) -> torch.Tensor:
-        x = self.embed(torch.cat([xt, x0], dim=-1))
+    def encode(self, tokens: torch.Tensor, mask, cos: torch.Tensor,
+               sin: torch.Tensor) -> torch.Tensor:
+        """Logits of every position of ``tokens`` (batch, L) under ``mask`` (L, L) or None,
+        with the RoPE rows ``cos``, ``sin`` (L, head_dim / 2) of their positions."""
+        x = self.embed(tokens)
         for layer in self.layers:
-            x = layer(x, self.attn_mask, self.cos, self.sin)
-        return self.head(self.norm(x))[:, :self.n]
+            x = layer(x, mask, cos, sin)
+        return self.head(self.norm(x))
+
+    def forward(self, xt: torch.Tensor, x0: torch.Tensor) -> torch.Tensor:
+        return self.encode(torch.cat([xt, x0], dim=-1), self.attn_mask, self.cos,
+                           self.sin)[:, :self.n]
 
     def loss(self, xt: torch.Tensor, x0: torch.Tensor) -> torch.Tensor:
         """Mean cross-entropy over the masked positions (no host synchronisation)."""
