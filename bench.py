@@ -736,6 +736,10 @@ def run_ours(args) -> None:
         extra["decode"] = decode_extras(ops, dev, l2, peaks)
         extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
         extra["sampler"] = sampler_extras(dev, l2, peaks)
+        if world == 1:  # the generation-side rows (about 25 s; one GPU only)
+            extra["graph_step"] = graph_step_extras(dev, l2, peaks)
+            extra["train_step"] = train_step_extras(dev, l2, peaks)
+            extra["generation"] = generation_extras(dev, l2, peaks)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {
@@ -784,7 +788,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=("ours", "reference"))
-    ap.add_argument("--no-decode", action="store_true", help="skip the decode extras")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the decode, cache, sampler and generation-side extras")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--kernels-only", action="store_true",
                     help="time only the device steps (no bs=4 line, e2e, decode or CPU legs); "
