@@ -542,6 +542,39 @@ def generation_extras(dev, l2, peaks, reps: int = 10, world: int = 1, rank: int 
     return {"generation_b64_l1024": out}
 
 
+def mdlm_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """The MDLM variant of config 5 (one 1024-token block, 64 steps, no cache; every step
+    re-encodes the whole sequence bidirectionally) on the stand-in backbone: the library's
+    prefill attention + fused sampler at batch 64 and 16, and the reference's flow (PyTorch
+    attention, float64 sampler ops) at batch 16, where its (batch, 1024, 50258) float64
+    tensors stay near 3.3 GB each. tokens/s = batch * 1024 / run time (CUDA events, one run
+    after a short warm-up)."""
+    from bench.backbone import Backbone
+    from bench.generation import MDLMGeneration
+    L, steps, V = 1024, 64, 50258
+    torch.manual_seed(0)
+    model = Backbone(V, L, BS).to(dev).bfloat16().eval()
+
+    def timed(fn) -> float:
+        flush_l2(l2)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b)
+
+    out = {}
+    for name, batch, lib in (("ours_b64", 64, True), ("ours_b16", 16, True),
+                             ("reference_flow_b16", 16, False)):
+        MDLMGeneration(model, batch, L, steps=2, use_library=lib).run()  # warm-up
+        t = timed(MDLMGeneration(model, batch, L, steps, use_library=lib, seed=1).run)
+        out[name] = {"ms": round(t, 1), "tokens_per_s": round(batch * L / (t * 1e-3))}
+        torch.cuda.empty_cache()
+    out["speedup_b16"] = round(out["reference_flow_b16"]["ms"] / out["ours_b16"]["ms"], 2)
+    return {"mdlm_l1024_64_steps": out}
+
+
 def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
     """One denoising step of the block sampler at the generation config:
     B=64 sequences, a 16-token block, vocabulary 50258, bf16 logits (the backbone runs under
@@ -736,10 +769,11 @@ def run_ours(args) -> None:
         extra["decode"] = decode_extras(ops, dev, l2, peaks)
         extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
         extra["sampler"] = sampler_extras(dev, l2, peaks)
-        if world == 1:  # the generation-side rows (about 25 s; one GPU only)
+        if world == 1:  # the generation-side rows (about 30 s; one GPU only)
             extra["graph_step"] = graph_step_extras(dev, l2, peaks)
             extra["train_step"] = train_step_extras(dev, l2, peaks)
             extra["generation"] = generation_extras(dev, l2, peaks)
+            extra["mdlm"] = mdlm_extras(dev, l2, peaks)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {
@@ -798,7 +832,7 @@ def main():
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
     ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step",
-                                        "train_step", "generation"),
+                                        "train_step", "generation", "mdlm"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -821,7 +855,8 @@ def main():
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
         fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
               "live_decode": live_decode_extras, "graph_step": graph_step_extras,
-              "train_step": train_step_extras, "generation": generation_extras}[args.extra]
+              "train_step": train_step_extras, "generation": generation_extras,
+              "mdlm": mdlm_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)

@@ -121,6 +121,27 @@ def _log_softmax(x: torch.Tensor) -> torch.Tensor:
     return shifted - torch.log(torch.exp(shifted).sum(dim=-1, keepdim=True))
 
 
+def subs_log_probs(logits: torch.Tensor, block: torch.Tensor, mask_index: int) -> torch.Tensor:
+    """SUBS (model/subs.py:11-43): -1e6 on the [MASK] logit, log_softmax, and one-hot rows
+    for the tokens that are already unmasked."""
+    bias = torch.zeros(logits.shape[-1], device=logits.device, dtype=logits.dtype)
+    bias[mask_index] = NEG_INF
+    log_probs = _log_softmax(logits + bias)
+    carry = torch.full_like(log_probs, NEG_INF).scatter(-1, block.unsqueeze(-1), 0.0)
+    return torch.where((block != mask_index).unsqueeze(-1), carry, log_probs)
+
+
+def reference_step(logits: torch.Tensor, block: torch.Tensor, mask_index: int, t: float,
+                   s: float, generator: torch.Generator | None) -> torch.Tensor:
+    """The reference's ancestral update (sample/sampler.py:100-122, 11-34): float64 weights,
+    Gumbel-max over float64 uniforms, and the where() that keeps unmasked tokens."""
+    q = torch.exp(subs_log_probs(logits, block, mask_index)).double() * (1 - s / t)
+    q[..., mask_index] = s / t
+    u = torch.rand(q.shape, dtype=torch.float64, device=q.device, generator=generator)
+    new = torch.argmax(q / (EPS - torch.log(u + EPS)), dim=-1)
+    return torch.where(block != mask_index, block, new)
+
+
 class ReferenceGeneration:
     """The reference's cached sampling flow in eager PyTorch ops (see the module docstring)."""
 
@@ -152,14 +173,6 @@ class ReferenceGeneration:
             x = x + layer.down(F.gelu(layer.up(layer.norm2(x)), approximate="tanh"))
         return m.head(m.norm(x))
 
-    def _subs(self, logits, block):
-        mask_index = self.m.mask_index
-        bias = torch.zeros(logits.shape[-1], device=logits.device, dtype=logits.dtype)
-        bias[mask_index] = NEG_INF
-        log_probs = _log_softmax(logits + bias)
-        carry = torch.full_like(log_probs, NEG_INF).scatter(-1, block.unsqueeze(-1), 0.0)
-        return torch.where((block != mask_index).unsqueeze(-1), carry, log_probs)
-
     @torch.no_grad()
     def run(self) -> torch.Tensor:
         mask_index = self.m.mask_index
@@ -171,12 +184,47 @@ class ReferenceGeneration:
                                device=self.cos.device)
             for i in range(self.steps):
                 t, s = 1 - i / self.steps, 1 - (i + 1) / self.steps
-                log_probs = self._subs(self._forward(block, positions, cache, False), block)
-                q = torch.exp(log_probs).double() * (1 - s / t)
-                q[..., mask_index] = s / t
-                u = torch.rand(q.shape, dtype=torch.float64, device=q.device, generator=self.gen)
-                new = torch.argmax(q / (EPS - torch.log(u + EPS)), dim=-1)
-                block = torch.where(block != mask_index, block, new)
+                logits = self._forward(block, positions, cache, False)
+                block = reference_step(logits, block, mask_index, t, s, self.gen)
             self._forward(block, positions, cache, True)  # commit (the backbone with store)
             blocks.append(block)
         return torch.cat(blocks, dim=-1)
+
+
+class MDLMGeneration:
+    """The MDLM variant of the sampling loop (block size = the whole sequence, no cache):
+    every step re-encodes all ``length`` tokens with bidirectional attention and updates
+    the masked ones. With ``use_library`` the layers' attention is the block-causal prefill
+    kernel (``bsdfa`` with block_size = length, so every key is visible) and the step is
+    the fused sampler; otherwise PyTorch's ``F.scaled_dot_product_attention`` and the
+    reference's sampler ops (SUBS, float64 weights, Gumbel-max, where). Eager: at 1024
+    tokens per sequence each step is long enough that launches do not matter."""
+
+    def __init__(self, model: Backbone, batch: int, length: int, steps: int = 64,
+                 use_library: bool = True, seed: int = 0):
+        self.m, self.B, self.L, self.steps = model, batch, length, steps
+        self.use_library, self.seed = use_library, seed
+        dev = model.head.weight.device
+        cos, sin = rope_tables(model.embed.embedding_dim // model.n_heads, length, dev)
+        self.cos, self.sin = cos, sin
+
+    @torch.no_grad()
+    def run(self) -> torch.Tensor:
+        from bench import attention as ba
+        from bench import backbone as bb
+        from bd3attn.sampler import subs_sample_step
+        ba.install_attention("bsdfa" if self.use_library else "sdpa", block_size=self.L,
+                             modules=bb.ATTENTION)
+        mask_index = self.m.mask_index
+        dev = self.cos.device
+        x = torch.full((self.B, self.L), mask_index, dtype=torch.int64, device=dev)
+        gen_cpu = torch.Generator().manual_seed(self.seed)
+        gen_dev = torch.Generator(device=dev).manual_seed(self.seed)
+        for i in range(self.steps):
+            t, s = 1 - i / self.steps, 1 - (i + 1) / self.steps
+            logits = self.m.encode(x, None, self.cos, self.sin)
+            if self.use_library:
+                subs_sample_step(logits, x, mask_index, t, s, generator=gen_cpu, out=x)
+            else:
+                x = reference_step(logits, x, mask_index, t, s, gen_dev)
+        return x

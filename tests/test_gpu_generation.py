@@ -61,3 +61,28 @@ def test_reference_flow_runs(model):
     from bench.generation import ReferenceGeneration
     out = ReferenceGeneration(model, B, 2, STEPS, generator=torch.Generator(device="cuda").manual_seed(1)).run()
     assert out.shape == (B, 2 * BS) and bool(((out >= 0) & (out < V - 1)).all())
+
+
+def test_mdlm_variant(model):
+    """The MDLM loop (whole-sequence block, no cache): with the library's prefill attention
+    the per-step logits equal PyTorch attention's within bf16 tolerance, and every token is
+    unmasked at the end."""
+    from bench import attention as ba
+    from bench import backbone as bb
+    from bench.generation import MDLMGeneration
+    L = 128
+    out = MDLMGeneration(model, 2, L, steps=8, seed=5).run()
+    assert_device_ok()
+    assert out.shape == (2, L) and bool(((out >= 0) & (out < V - 1)).all())
+    x = out.clone()
+    x[:, ::3] = V - 1  # a partly masked sequence
+    gen = MDLMGeneration(model, 2, L, steps=1)
+    with torch.no_grad():
+        ba.install_attention("bsdfa", block_size=L, modules=bb.ATTENTION)
+        ours = model.encode(x, None, gen.cos, gen.sin).float()
+        ba.install_attention("sdpa", modules=bb.ATTENTION)
+        ref = model.encode(x, None, gen.cos, gen.sin).float()
+    err = (ours - ref).abs().max().item()
+    assert err <= 0.03 * max(1.0, ref.abs().max().item()), err
+    ref_out = MDLMGeneration(model, 2, L, steps=8, use_library=False, seed=5).run()
+    assert bool(((ref_out >= 0) & (ref_out < V - 1)).all())
