@@ -106,6 +106,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 constexpr int kChunk = 8;               // entries of a 16-byte chunk of a bf16 row
+constexpr int kWalkChunks = 32;         // chunks per thread the parallel walk holds (V <= 131072)
 constexpr uint16_t kBf16NegInf = 0xFF80u;
 
 __device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) {
@@ -205,6 +206,8 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   __shared__ double wscan[kSampleThreads / 32];
   __shared__ double last_incl[kSampleThreads / 32];
   __shared__ int ri[kSampleThreads / 32];
+  __shared__ double walk_q[kWalkChunks * kChunk];  // the claimed slice's weights
+  __shared__ int walk_owner;
   const int row = blockIdx.x;
   const int b = row / p.S, i = row % p.S;
   const long long tok = p.xt[static_cast<long long>(b) * p.S + i];
@@ -399,7 +402,43 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     double target = u53(r.x, r.y) * total;
     if (target >= total) target = nextafter(total, 0.0);
     int mine = 0x7fffffff;
-    if (excl <= target && target < incl) {  // this thread's slice: walk it chunk by chunk,
+    const bool claim = excl <= target && target < incl;
+    // The slices tile [0, total) exactly (each excl is the previous thread's incl), so one
+    // thread claims the target. Its chunks' weights are then computed by one thread each
+    // into shared memory, and the claimant adds them up in its own order (the additions
+    // and so the token are those of a walk by the claimant alone, which is the fallback).
+    const int per_thread = (n_chunks + kSampleThreads - 1) / kSampleThreads;
+    if (__syncthreads_count(claim) == 1 && per_thread <= kWalkChunks) {
+      if (claim) walk_owner = static_cast<int>(threadIdx.x);
+      __syncthreads();
+      const int owner = walk_owner;
+      if (static_cast<int>(threadIdx.x) < per_thread) {
+        const int c = owner + static_cast<int>(threadIdx.x) * kSampleThreads;
+        if (c < n_chunks) {
+          double q[kChunk];
+          chunk_q(c, q);
+#pragma unroll
+          for (int k = 0; k < kChunk; ++k) walk_q[threadIdx.x * kChunk + k] = q[k];
+        }
+      }
+      __syncthreads();
+      if (claim) {
+        const double local = target - excl;
+        double acc = 0.0;
+        int last_nz = 0x7fffffff;
+        for (int i = 0, c = owner; c < n_chunks && mine == 0x7fffffff; ++i, c += kSampleThreads) {
+#pragma unroll
+          for (int k = 0; k < kChunk; ++k) {
+            if (mine != 0x7fffffff) continue;
+            const double q = walk_q[i * kChunk + k];
+            acc += q;
+            if (q > 0.0) last_nz = c * kChunk + k;
+            if (local < acc) mine = c * kChunk + k;
+          }
+        }
+        if (mine == 0x7fffffff) mine = last_nz;  // the local offset rounded past the slice
+      }
+    } else if (claim) {  // this thread's slice: walk it chunk by chunk,
       const double local = target - excl;  // adding in the same order as part
       double acc = 0.0;
       int last_nz = 0x7fffffff;
