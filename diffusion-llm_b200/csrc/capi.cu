@@ -8,6 +8,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
 
 #include "../../include/bd3_attn.h"
 #include "attn_bwd.cuh"
@@ -161,6 +162,26 @@ struct ProfScope {
 int check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? BD3_OK : cuda_fail(e, what);
+}
+
+// Launch with programmatic stream serialization: the kernel may begin while the previous
+// kernel on the stream finishes, and orders itself after it with griddep_wait (the decode
+// and combine kernels do so before reading anything the previous kernel writes).
+template <typename... Params, typename... Args>
+int launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+               cudaStream_t stream, const char* what, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e == cudaSuccess ? check_launch(what) : cuda_fail(e, what);
 }
 
 // Bind the current device's primary context to this host thread. A thread that has only
@@ -507,9 +528,10 @@ int launch_decode(bool live, const void* q, const void* k, const void* v, void* 
   if ((rc = set_smem(kern, bd3::DecSmem::kAlloc, slot)) != BD3_OK) return rc;
   {
     ProfScope ps(kPfDecode, stream);
-    kern<<<grid, bd3::kDecThreads, bd3::DecSmem::kAlloc, stream>>>(tq, tk, tv, p);
+    if ((rc = launch_pdl(kern, grid, dim3(bd3::kDecThreads), bd3::DecSmem::kAlloc, stream,
+                         "decode_kernel launch", tq, tk, tv, p)) != BD3_OK)
+      return rc;
   }
-  if ((rc = check_launch("decode_kernel launch")) != BD3_OK) return rc;
   if (n_splits > 1) {
     bd3::CombineParams c{};
     c.parts = p.ws_o;
@@ -530,8 +552,9 @@ int launch_decode(bool live, const void* q, const void* k, const void* v, void* 
     c.out_dtype = out_dtype;
     const int64_t threads = B * H * q_len * 8;
     ProfScope ps(kPfCombine, stream);
-    bd3::decode_combine_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(c);
-    if ((rc = check_launch("decode_combine_kernel launch")) != BD3_OK) return rc;
+    if ((rc = launch_pdl(bd3::decode_combine_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)),
+                         dim3(256), 0, stream, "decode_combine_kernel launch", c)) != BD3_OK)
+      return rc;
   }
   return BD3_OK;
 }

@@ -327,6 +327,16 @@ __device__ __forceinline__ float2 exp2_fma2(float2 t) {
 
 // Round a float through dtype kDtype (0 bf16, 1 fp16, 2 fp32: identity) and back, as a
 // PyTorch elementwise op on tensors of that dtype rounds its fp32 result.
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization
+// attribute may start while the kernel before it on the stream is still running, once every
+// CTA of that kernel has called griddep_launch_dependents (or exited); griddep_wait then
+// blocks until that kernel has completed and its memory is visible. Without the attribute
+// (or after a kernel that never triggers) both are no-ops in effect.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <int kDtype>
 __device__ __forceinline__ float rnd(float x) {
   if constexpr (kDtype == 0) return __bfloat162float(__float2bfloat16_rn(x));

@@ -129,6 +129,10 @@ __global__ void __launch_bounds__(kDecThreads)
   // those keys, key 0 at position 0, and the key tiles are spread over all n_splits again.
   // A count outside [q_len, capacity] is clamped and raises status bit 2. A CUDA graph
   // captured once thus serves a cache that grows between replays.
+  // Launched after the QKV/RoPE cache write with programmatic serialization: wait for it
+  // (q and the block's K/V rows) before any global read, and let the combine launch early.
+  griddep_wait();
+  griddep_launch_dependents();
   DecParams p = p_in;
   if (!kLive && p.kv_len_dev != nullptr) {
     int kl = *p.kv_len_dev;
@@ -424,6 +428,7 @@ struct CombineParams {
 };
 
 __global__ void __launch_bounds__(256) decode_combine_kernel(const CombineParams p) {
+  griddep_wait();  // the partials of the decode launched just before (see decode_kernel)
   const int idx = blockIdx.x * blockDim.x + threadIdx.x;
   const int per_bh = p.rows * 8;
   if (idx >= p.n_bh * per_bh) return;

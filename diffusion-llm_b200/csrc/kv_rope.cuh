@@ -83,6 +83,7 @@ __device__ __forceinline__ void store8(void* base, long long i, const float (&x)
 // and [8t + D/2, 8t + D/2 + 8)), every access a 16-byte piece (two for fp32).
 template <int kDtype>
 __global__ void __launch_bounds__(256) qkv_rope_cache_kernel(const RopeCacheParams p) {
+  griddep_launch_dependents();  // the decode after it may launch now and wait for it there
   const int groups = p.D / 16;  // threads per (batch, token, head)
   const long long gid = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   const long long units = static_cast<long long>(p.B) * p.S * p.H * groups;
