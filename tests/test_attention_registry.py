@@ -79,3 +79,22 @@ def test_backbone_routes_attention_and_trains_on_cpu():
         del ba.BACKENDS["counting"]
     assert calls == [(64, 64), (64, 64)]
     assert torch.isfinite(loss) and model.layers[0].qkv.weight.grad is not None
+
+
+def test_reference_generation_flows_run_on_cpu():
+    """The reference-flow generators (the comparison arms of the generation benchmark) run
+    on the CPU with a tiny backbone: every generated token is a real token."""
+    from bench.backbone import Backbone
+    from bench.generation import MDLMGeneration, ReferenceGeneration, subs_log_probs
+    torch.manual_seed(0)
+    model = Backbone(100, 32, 8, d_model=64, n_heads=1, n_layers=1, d_ff=128).eval()
+    ref = ReferenceGeneration(model, 2, 3, 4, generator=torch.Generator().manual_seed(1))
+    out = ref.run()
+    assert out.shape == (2, 24) and bool(((out >= 0) & (out < 99)).all())
+    out = MDLMGeneration(model, 2, 32, steps=4, use_library=False).run()
+    assert out.shape == (2, 32) and bool(((out >= 0) & (out < 99)).all())
+    # SUBS: [MASK] gets no mass; unmasked rows are one-hot at their token
+    logits = torch.randn(1, 2, 100)
+    lp = subs_log_probs(logits, torch.tensor([[99, 5]]), 99)
+    assert lp[0, 0, 99] < -1e5 and torch.allclose(lp[0, 0].exp().sum(), torch.tensor(1.0))
+    assert lp[0, 1, 5] == 0 and bool((lp[0, 1, torch.arange(100) != 5] == -1e6).all())
