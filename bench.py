@@ -489,8 +489,13 @@ def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
                                 weight_decay=0.0)
         for i in range(3):
             bb.train_step(model, opt, *batches[i % 4])
-        it = iter(range(10 ** 9))
-        ms = time_steps(lambda: bb.train_step(model, opt, *batches[next(it) % 4]), reps, l2)
+        count = [0]
+
+        def one_step():
+            count[0] += 1
+            bb.train_step(model, opt, *batches[count[0] % 4])
+
+        ms = time_steps(one_step, reps, l2)
         t = statistics.median(ms)
         out[name] = {"ms_per_step": round(t, 2), "tokens_per_s": round(Bt * n / (t * 1e-3))}
         del model, opt
