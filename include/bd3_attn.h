@@ -91,6 +91,9 @@ BD3_API int bd3_attn_bwd(const void* q, const void* k, const void* v, const void
  *   strides[12] = q, k, v, o (batch, head, seq) in elements.
  *   lse_out: optional (B*H, q_len) fp32 natural-log LSE of each row (NULL to skip).
  * bd3_decode_plan() picks n_splits (pass the result back) and the workspace size.
+ * The split-KV kernel and the combine are launched with programmatic stream serialization:
+ * they may start while the previous kernel on the stream finishes but wait for it before
+ * reading or writing any memory, so stream order is as for any launch.
  */
 BD3_API int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t block_size,
                     int64_t q_pos0, int64_t kv_pos0, int64_t* n_splits, size_t* workspace_bytes);
