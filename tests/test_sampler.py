@@ -121,3 +121,32 @@ def test_capi_sampler_device_args_checks():
     assert call(rng=None) == BD3_ERR_INVALID
     assert call(dtype=1) == BD3_ERR_INVALID
     assert call(mask=100) == BD3_ERR_INVALID
+
+
+@pytest.mark.parametrize("V", [1, 7, 8, 9, 4096, 4097, 50258])
+def test_thread_order_partitions_the_row(V):
+    """The kernel's element order visits every entry exactly once, in 8-entry chunks."""
+    order = [j for t in range(512) for j in osm.thread_order(V, t)]
+    assert sorted(order) == list(range(V))
+    for t in (0, 1, 511):
+        mine = osm.thread_order(V, t)
+        assert all(j // 8 % 512 == t for j in mine)
+
+
+def test_inverse_cdf_single_nonzero_weight():
+    """A row with one nonzero weight draws it for every uniform, including the extremes."""
+    q = np.zeros(1000)
+    q[637] = 0.25
+    for r in (0.0, 0.5, 1 - 2 ** -53):
+        j, _ = osm.inverse_cdf(q, r)
+        assert j == 637
+
+
+def test_subs_weights_step_structure():
+    """q at [MASK] is s/t; the others are exp(log-softmax) * (1 - s/t), summing to it."""
+    rng = np.random.default_rng(2)
+    logits = rng.standard_normal((3, 50)).astype(np.float32)
+    t, s = 0.8, 0.3
+    q = osm.subs_weights(logits, 49, t, s, "f32")
+    assert np.allclose(q[:, 49], s / t)
+    assert np.allclose(q[:, :49].sum(-1), 1 - s / t, rtol=1e-5)
