@@ -39,9 +39,8 @@ UNIT = "TFLOP/s"
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each training
-# kernel on the C2 workload at B=8, from one `ncu --set full` capture (summarised in
-# profiles/bwd_fused_c2.md and profiles/attn_fwd_c2.md). The work is B x H independent
-# (batch, head) slices, so the traffic scales with B.
+# kernel on the C2 workload at B=8, from one `ncu --set full` capture of that kernel. The
+# work is B x H independent (batch, head) slices, so the traffic scales with B.
 NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 319_690_752, "attn_fwd": 82_574_336}
 
 
@@ -324,6 +323,122 @@ def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
     return out
 
 
+def c1_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """Benchmark config 1: the training forward on fp32 inputs (B=2, H=12, n=1024, bs=16,
+    N(0,1)) through BlockSparseFlashAttention.apply, which scales the fp32 tensors by powers
+    of two into fp16 (tf32's 11-bit significand), runs the fp16 forward kernel and returns
+    fp32 O; and the forward kernel alone on the scaled operands. Useful FLOPs 4*D*nnz*B*H."""
+    from bd3attn import ops
+    from kernels import _precision
+    from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+    b, n, bs = 2, 1024, 16
+    g = torch.Generator().manual_seed(21)
+    q, k, v = (torch.randn(b, H, 2 * n, D, generator=g).to(dev) for _ in range(3))
+    with torch.no_grad():
+        for _ in range(3):
+            BlockSparseFlashAttention.apply(q, k, v, bs)
+        api = statistics.median(time_steps(lambda: BlockSparseFlashAttention.apply(q, k, v, bs),
+                                           reps, l2))
+        q16, k16, v16, _, _ = _precision.qkv_to_f16(q, k, v)
+        kern = statistics.median(time_steps(lambda: ops.attn_fwd_raw(q16, k16, v16, bs), reps, l2))
+    fl = 4.0 * D * nnz(n, bs) * b * H
+    return {"c1_fp32_fwd_b2": {"api_us": round(api * 1e3, 2), "kernel_us": round(kern * 1e3, 2),
+                               "useful_gflop": round(fl / 1e9, 3),
+                               "api_tflops": round(fl / (api * 1e-3) / 1e12, 2),
+                               "kernel_tflops": round(fl / (kern * 1e-3) / 1e12, 2),
+                               "operands": "fp16 after exact power-of-two scaling (tf32 "
+                                           "significand), fp32 accumulate, fp32 O"}}
+
+
+def decode_grid_extras(dev, l2, peaks, reps: int = 10) -> dict:
+    """Benchmark config 3's whole grid on one GPU: split-KV decode of a 16-token query block
+    (H=12, head_dim 64, bf16) over a cache of N in {1K, 4K, 16K, 64K} keys plus the block
+    itself, at batch {1, 8, 32}; splits from the library's planner. Algorithmic bytes:
+    B * H * (256 * kv_len + 4096) (K and V read once, q read and O written once)."""
+    from bd3attn import ops
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(5)
+    for n in (1024, 4096, 16384, 65536):
+        kv = n + 16
+        kmax = torch.empty(32, H, kv, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        vmax = torch.empty_like(kmax).normal_(generator=g)
+        for b in (1, 8, 32):
+            q = torch.empty(b, H, 16, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+            k, v = kmax[:b], vmax[:b]
+            for _ in range(3):
+                ops.decode_raw(q, k, v, BS)
+            t = statistics.median(time_steps(lambda: ops.decode_raw(q, k, v, BS), reps, l2))
+            by = b * H * (256 * kv + 4096)
+            ns, _ = ops.decode_plan(b, H, 16, kv, BS)
+            out[f"b{b}_kv{n // 1024}k"] = {"us": round(t * 1e3, 2),
+                                           "GBps": round(by / t / 1e6, 1),
+                                           "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4),
+                                           "n_splits": ns}
+        del kmax, vmax
+    return out
+
+
+def sharded_decode_extras(dev, l2, peaks, world: int, rank: int, reps: int = 10) -> dict:
+    """Benchmark config 3 at 64K keys, sequence-sharded over the ranks (north_star's
+    long-context decode): B=32, H=12, a 16-token query block at the end of a 64K + 16 key
+    cache. Rank r holds keys [seq_shard(r)) (contiguous, 64-aligned), decodes its slice into
+    a partial (O fp32, LSE) with the library's kernel, one NCCL all-gather moves every rank's
+    packed [O | LSE] (B*H*16*65 fp32, 1.6 MB), and bd3_lse_merge combines them
+    (bd3attn.dist.sharded_decode). Strong scaling: the cache is fixed, so each rank reads
+    1/world of it. The step time is the max over ranks of the median step; bytes are the
+    whole cache's. Rank 0 checks the merged O and LSE against a single-GPU decode of the
+    whole cache (the same seeded tensors exist on every rank)."""
+    from bd3attn import ops
+    from bd3attn.dist import seq_shard, sharded_decode
+    b, kv = 32, 65536 + 16
+    g = torch.Generator(device=dev).manual_seed(17)  # identical on every rank
+    q = torch.empty(b, H, 16, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    k = torch.empty(b, H, kv, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    v = torch.empty_like(k).normal_(generator=g)
+    a, e = seq_shard(kv, world, rank)
+    k_loc, v_loc = k[:, :, a:e], v[:, :, a:e]
+
+    if world > 1:
+        def step():
+            return sharded_decode(q, k_loc, v_loc, BS, a, kv, out_dtype=torch.float32)
+    else:
+        def step():
+            return ops.decode_raw(q, k, v, BS, out_dtype=torch.float32, return_lse=True)
+    for _ in range(3):
+        step()
+    barrier(world)
+    t = max_over_ranks(statistics.median(time_steps(step, reps, l2)), world)
+    out = {"gpus": world, "scaling": "strong", "keys_per_rank": e - a,
+           "us": round(t * 1e3, 2)}
+    by = b * H * (256 * kv + 4096)
+    out["GBps"] = round(by / t / 1e6, 1)
+    out["frac_hbm_aggregate"] = round(by / t / 1e6 / (world * peaks["hbm_gbs"]), 4)
+    if world > 1:
+        import torch.distributed as dist
+        packed = torch.empty(b, H, 16 * 65, dtype=torch.float32, device=dev)
+        gathered = torch.empty(world * b, H, 16 * 65, dtype=torch.float32, device=dev)
+        for _ in range(3):
+            dist.all_gather_into_tensor(gathered, packed)
+        barrier(world)
+        ag = max_over_ranks(statistics.median(time_steps(
+            lambda: dist.all_gather_into_tensor(gathered, packed), reps, l2)), world)
+        local = statistics.median(time_steps(
+            lambda: ops.decode_raw(q, k_loc, v_loc, BS, q_pos0=kv - 16, kv_pos0=a,
+                                   out_dtype=torch.float32, return_lse=True), reps, l2))
+        out["allgather_us"] = round(ag * 1e3, 2)
+        out["local_partial_us"] = round(max_over_ranks(local, world) * 1e3, 2)
+        o, lse = step()
+        if rank == 0:
+            o_ref, lse_ref = ops.decode_raw(q, k, v, BS, out_dtype=torch.float32,
+                                            return_lse=True)
+            eo = (o - o_ref).abs().max().item()
+            el = (lse - lse_ref).abs().max().item()
+            out["check"] = {"vs": "single-GPU decode of the whole cache", "o_max_abs": eo,
+                            "lse_max_abs": el, "tol": 1e-3, "ok": eo <= 1e-3 and el <= 1e-3}
+        barrier(world)
+    return {"splitkv_b32_kv64k_seq_sharded": out}
+
+
 def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
     """Benchmark config 4 alone (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per
     (b, h)), as decode_extras times it: the command the live-block ncu capture runs."""
@@ -474,8 +589,7 @@ def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     tokens/s = batch * seq_len / median step time, the reference's formula (:294)."""
     import copy
 
-    from bench import attention as ba
-    from bench import backbone as bb
+    from workloads import backbone as bb
     Bt, n, bs, V = 16, 1024, 16, 50258
     torch.manual_seed(0)
     base = bb.Backbone(V, n, bs).to(dev)
@@ -484,7 +598,7 @@ def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     out = {}
     for name in ("bsfa", "sdpa"):
         model = copy.deepcopy(base)
-        ba.install_attention(name, block_size=bs, modules=bb.ATTENTION)
+        bb.use_attention(name, block_size=bs)
         opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.999),
                                 weight_decay=0.0)
         for i in range(3):
@@ -504,20 +618,21 @@ def train_step_extras(dev, l2, peaks, reps: int = 10) -> dict:
     return {"train_step_b16_n1024": out}
 
 
-def generation_extras(dev, l2, peaks, reps: int = 10, world: int = 1, rank: int = 0) -> dict:
+def generation_extras(dev, l2, peaks, reps: int = 10, world: int = 1, rank: int = 0,
+                      with_reference: bool = True) -> dict:
     """Benchmark config 5 with the stand-in backbone (12 layers, d_model 768, 12 heads, d_ff
-    3072, vocabulary 50258, bf16 weights, random init): 64 sequences generated to 1024 tokens
-    in 16-token blocks, 16 sampler steps per block, through bench/generation.py's
+    3072, vocabulary 50258, bf16 weights, random init): sequences generated to 1024 tokens in
+    16-token blocks, 16 sampler steps per block, through workloads/generation.py's
     CachedGeneration (in-place cache, split-KV decode, fused sampler, one CUDA graph replay
     per block) and, on one GPU, ReferenceGeneration (the reference's flow in eager PyTorch
-    ops). Under torchrun the batch is split over the ranks (64 / world sequences each, no
-    communication) and the time is the max over ranks, so tokens/s is the whole job's.
-    tokens/s = 64 * 1024 / time (CUDA events; ours is timed after a run that captures its
-    graph)."""
-    from bench.backbone import Backbone
-    from bench.generation import CachedGeneration, ReferenceGeneration
+    ops). Two partitions over the ranks, with weight replicas and no communication:
+    "strong", the config's 64 sequences split by batch (64 / world per rank), and "weak", 64
+    sequences per rank (64 * world in all). The time is the max over ranks of the run, so
+    tokens/s = sequences * 1024 / time is the whole job's (CUDA events; each run is timed
+    after one that captures its graph)."""
+    from workloads.backbone import Backbone
+    from workloads.generation import CachedGeneration, ReferenceGeneration
     Bg, n_blocks, steps, V = 64, 64, 16, 50258
-    b_local = Bg // world
     torch.manual_seed(0)  # the same weights on every rank
     model = Backbone(V, 1024, BS).to(dev).bfloat16().eval()
 
@@ -531,19 +646,26 @@ def generation_extras(dev, l2, peaks, reps: int = 10, world: int = 1, rank: int 
         torch.cuda.synchronize()
         return max_over_ranks(a.elapsed_time(b), world)
 
-    ours = CachedGeneration(model, b_local, n_blocks, steps, seed=1 + rank)
-    ours.run()
-    t_ours = statistics.median([timed(ours.run) for _ in range(2)])
-    toks = Bg * n_blocks * BS
-    out = {"gpus": world, "sequences_per_gpu": b_local,
-           "ours": {"ms": round(t_ours, 1), "tokens_per_s": round(toks / (t_ours * 1e-3))}}
-    if world == 1:
+    out = {"gpus": world}
+    parts = [("strong", Bg // world)] + ([("weak", Bg)] if world > 1 else [])
+    for name, b_local in parts:
+        ours = CachedGeneration(model, b_local, n_blocks, steps, seed=1 + rank)
+        ours.run()
+        t = statistics.median([timed(ours.run) for _ in range(2)])
+        toks = b_local * world * n_blocks * BS
+        out[name] = {"sequences_per_gpu": b_local, "sequences": b_local * world,
+                     "ms": round(t, 1), "tokens_per_s": round(toks / (t * 1e-3))}
+        del ours
+        torch.cuda.empty_cache()
+    out["ours"] = out["strong"]  # the config's 64 sequences
+    if world == 1 and with_reference:
+        toks = Bg * n_blocks * BS
         ReferenceGeneration(model, Bg, 1, steps).run()  # warm-up (library set-up)
         t_ref = timed(ReferenceGeneration(model, Bg, n_blocks, steps,
                                           generator=torch.Generator(device=dev).manual_seed(1)).run)
         out["reference_flow"] = {"ms": round(t_ref, 1),
                                  "tokens_per_s": round(toks / (t_ref * 1e-3))}
-        out["speedup"] = round(t_ref / t_ours, 2)
+        out["speedup"] = round(t_ref / out["strong"]["ms"], 2)
     return {"generation_b64_l1024": out}
 
 
@@ -554,8 +676,8 @@ def mdlm_extras(dev, l2, peaks, reps: int = 10) -> dict:
     attention, float64 sampler ops) at batch 16, where its (batch, 1024, 50258) float64
     tensors stay near 3.3 GB each. tokens/s = batch * 1024 / run time (CUDA events, one run
     after a short warm-up)."""
-    from bench.backbone import Backbone
-    from bench.generation import MDLMGeneration
+    from workloads.backbone import Backbone
+    from workloads.generation import MDLMGeneration
     L, steps, V = 1024, 64, 50258
     torch.manual_seed(0)
     model = Backbone(V, L, BS).to(dev).bfloat16().eval()
@@ -715,6 +837,38 @@ def run_ours(args) -> None:
 
     link = {"h2d": round(link_gbps(dbuf[0][0], host[0]), 1),
             "d2h": round(link_gbps(outs[0][0], dbuf[0][0]), 1)}
+
+    def concurrent_link(reps: int = 3) -> dict:
+        """The host link as the e2e steps use it: every rank copies one step's inputs in
+        (4 tensors) and, at the same time on a second stream, one step's gradients out (3
+        tensors), all ranks at once after a barrier. Returns the whole job's GB/s each way
+        (bytes of all ranks / the slowest rank's time) and the time per step this implies
+        when the copies alone set the pace."""
+        h2d_s, d2h_s = torch.cuda.Stream(), torch.cuda.Stream()
+        times = []
+        for _ in range(reps):
+            barrier(world)
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record(h2d_s)
+            ev[2].record(d2h_s)
+            with torch.cuda.stream(h2d_s):
+                for dst, src in zip(dbuf[0], host):
+                    dst.copy_(src, non_blocking=True)
+            with torch.cuda.stream(d2h_s):
+                for dst, src in zip(outs[0], dbuf[1][:3]):
+                    dst.copy_(src, non_blocking=True)
+            ev[1].record(h2d_s)
+            ev[3].record(d2h_s)
+            torch.cuda.synchronize()
+            times.append((ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])))
+        h2d_ms = max_over_ranks(statistics.median(t for t, _ in times), world)
+        d2h_ms = max_over_ranks(statistics.median(t for _, t in times), world)
+        nb = q.numel() * q.element_size()
+        return {"ranks": world, "h2d_GBps_job": round(4 * nb * world / h2d_ms / 1e6, 1),
+                "d2h_GBps_job": round(3 * nb * world / d2h_ms / 1e6, 1),
+                "copy_bound_ms_per_step": round(max(h2d_ms, d2h_ms), 4)}
+
+    link_job = concurrent_link()
     for bset in dbuf:
         for t in bset[:3]:
             t.requires_grad_(True)
@@ -771,13 +925,18 @@ def run_ours(args) -> None:
                  4.0 * B * H * (2 * N_HALF) ** 2 * D / (prof["attn_fwd"][0] / prof["attn_fwd"][1]
                                                          * 1e-3) / 1e12, 2)}
     if not args.no_decode:
-        extra["decode"] = decode_extras(ops, dev, l2, peaks)
-        extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
-        extra["sampler"] = sampler_extras(dev, l2, peaks)
-        if world == 1:  # the generation-side rows (about 30 s; one GPU only)
+        # rows measured at every N: config 3's 64K decode sequence-sharded over the ranks
+        # (one NCCL all-gather per step) and config 5's generation split by batch
+        extra["sharded_decode"] = sharded_decode_extras(dev, l2, peaks, world, rank)
+        extra["generation"] = generation_extras(dev, l2, peaks, world=world, rank=rank)
+        if world == 1:  # single-GPU rows
+            extra["decode"] = decode_extras(ops, dev, l2, peaks)
+            extra["decode_grid"] = decode_grid_extras(dev, l2, peaks)
+            extra["c1"] = c1_extras(dev, l2, peaks)
+            extra["kv_cache"] = kv_cache_extras(dev, l2, peaks)
+            extra["sampler"] = sampler_extras(dev, l2, peaks)
             extra["graph_step"] = graph_step_extras(dev, l2, peaks)
             extra["train_step"] = train_step_extras(dev, l2, peaks)
-            extra["generation"] = generation_extras(dev, l2, peaks)
             extra["mdlm"] = mdlm_extras(dev, l2, peaks)
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
@@ -807,6 +966,9 @@ def run_ours(args) -> None:
                     "timing": "one region over all steps; copies in/out on their own streams "
                               "overlap the neighbouring steps' compute (double-buffered inputs)",
                     "link_GBps": link,
+                    "link_all_ranks": link_job,
+                    "frac_of_copy_bound": round(link_job["copy_bound_ms_per_step"]
+                                                / (e2e_ms / args.steps), 4),
                     "pinned_on": (f"{len(local_cpus)} GPU-local cores" if local_cpus
                                   else "any core (NVML gave no affinity)")},
             "gpu_launches": launches,
@@ -837,18 +999,22 @@ def main():
                     help="time only the decode rows (split-KV B=8 x 16K cache, live blocks); "
                          "the command the decode ncu captures run")
     ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step",
-                                        "train_step", "generation", "mdlm"),
+                                        "train_step", "generation", "mdlm", "sharded_decode",
+                                        "decode_grid", "c1"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
     elif args.decode_only:
         run_decode_only(args)
-    elif args.extra == "generation":
+    elif args.extra in ("generation", "sharded_decode"):
         world, rank, local = dist_setup(args.gpus)
         dev = torch.device("cuda", local)
         l2 = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
-        res = generation_extras(dev, l2, load_peaks(), world=world, rank=rank)
+        if args.extra == "generation":
+            res = generation_extras(dev, l2, load_peaks(), world=world, rank=rank)
+        else:
+            res = sharded_decode_extras(dev, l2, load_peaks(), world, rank)
         if rank == 0:
             print(json.dumps(res), flush=True)
         if world > 1:
@@ -861,7 +1027,8 @@ def main():
         fn = {"kv_cache": kv_cache_extras, "sampler": sampler_extras,
               "live_decode": live_decode_extras, "graph_step": graph_step_extras,
               "train_step": train_step_extras, "generation": generation_extras,
-              "mdlm": mdlm_extras}[args.extra]
+              "mdlm": mdlm_extras, "decode_grid": decode_grid_extras,
+              "c1": c1_extras}[args.extra]
         print(json.dumps(fn(dev, l2, load_peaks(), reps=max(args.steps, 1))), flush=True)
     else:
         run_ours(args)

@@ -304,7 +304,10 @@ __device__ __forceinline__ float max64(const float (&x)[64]) {
 // Range reduction after Cody and Waite: t = j + f with j = floor(t) and f in [0, 1), so
 // 2^t = 2^j * 2^f; 2^j is added to the exponent field and 2^f is a cubic
 // p(f) = 1 + f (c1 + f (c2 + f c3)). The coefficients minimise the maximum relative error on
-// [0, 1) (Lawson's iteratively reweighted least squares, fit_exp2.py beside this file):
+// [0, 1): a weighted least-squares fit of (2^f - 1) / 2^f by f (c1 + f (c2 + f c3)) / 2^f on
+// 20000 points of (0, 1], its weights updated by Lawson's iteration (each weight times its
+// point's absolute residual, renormalised) until the residual equioscillates, the result
+// rounded to fp32. Maximum relative error of the fp32 evaluation:
 // 8.6e-5, under half an ulp of bf16 and fp16 (the P operand's types). The floor comes from
 // adding 1.5 * 2^23 with rounding toward -inf, which leaves floor(t) in the low mantissa bits.
 // t is clamped to -127 first: there j = -127 and p(0) = 1, so the result's bits are exactly 0

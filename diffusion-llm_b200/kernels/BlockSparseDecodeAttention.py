@@ -9,12 +9,16 @@ sampler) run the tcgen05 kernel of csrc/attn_fwd.cuh in its block-causal mode.
 
 Added here (no counterpart in the reference): ``block_sparse_live_decode_attention`` reads
 only the KV blocks listed live for each (batch, head).
+
+fp32 inputs run on the fp16 kernels at tf32's operand precision (kernels/_precision.py), and
+the output comes back as fp32.
 """
 
 import torch
 from torch import Tensor
 
 from bd3attn import ops
+from kernels import _precision
 
 
 def _last_stride_1(x: Tensor) -> Tensor:
@@ -37,13 +41,29 @@ def block_sparse_decode_attention(
     B, H, q_len, D = q.shape
     kv_len = k.shape[2]
     assert q_len <= kv_len, "queries are the last q_len key positions"
+    return _decode(q, k, v, block_size)
+
+
+def _decode(q: Tensor, k: Tensor, v: Tensor, block_size: int) -> Tensor:
+    """The library's block-causal decode (split-KV for q_len <= 64, the tcgen05 prefill
+    kernel above), on 16-bit operands; fp32 inputs through the exact power-of-two scaling."""
     out_dtype = q.dtype
-    cdt = _cdt(q, k, v)
-    q, k, v = _last_stride_1(q.to(cdt)), _last_stride_1(k.to(cdt)), _last_stride_1(v.to(cdt))
+    if q.dtype == k.dtype == v.dtype == torch.float32:
+        q, k, v, _, c = _precision.qkv_to_f16(q, k, v)
+        # decode blocks return fp32 directly; prefill writes the operand dtype
+        odt = torch.float32 if q.shape[2] <= 64 else torch.float16
+    else:
+        cdt = _cdt(q, k, v)
+        q, k, v, c, odt = q.to(cdt), k.to(cdt), v.to(cdt), None, None
+    q, k, v = _last_stride_1(q), _last_stride_1(k), _last_stride_1(v)
     if torch.compiler.is_compiling():
         o = torch.ops.bd3.decode(q, k, v, int(block_size))
+        if c is not None:
+            return _precision.scaled_back(o, c)
     else:
-        o = ops.decode_raw(q, k, v, int(block_size))
+        o = ops.decode_raw(q, k, v, int(block_size), out_dtype=odt)
+        if c is not None:
+            return _precision.scaled_back(o, c)
     return o if o.dtype == out_dtype else o.to(out_dtype)
 
 

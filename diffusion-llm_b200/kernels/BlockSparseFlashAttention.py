@@ -6,9 +6,11 @@ assertions (:474-476, :487, :522) and the same saved tensors (q, k, v, O, L), wh
 per-row natural-log LSE of shape (B, H, 2n) in fp32 (:482, :169). The forward is the
 tcgen05 kernel of csrc/attn_fwd.cuh, the backward the three kernels of csrc/attn_bwd.cuh.
 
-Inputs are 16-bit (bf16 or f16), which is what autocast hands the model's attention. fp32
-inputs (the reference's Triton path computes them with tf32 dots) are rounded to bf16 for
-the kernels and the results cast back to fp32.
+Inputs are 16-bit (bf16 or f16), which is what autocast hands the model's attention, or fp32.
+The reference's Triton path computes fp32 inputs with tf32 dots (11-bit significands, fp32
+accumulation); here they run on the fp16 kernels, whose operands have the same 11-bit
+significand, after an exact power-of-two scaling into fp16's range (kernels/_precision.py),
+and O, dQ, dK, dV come back as fp32. Mixed input dtypes run in bf16.
 """
 
 from typing import Any
@@ -17,6 +19,7 @@ import torch
 from torch import Tensor
 
 from bd3attn import ops
+from kernels import _precision
 
 
 def _compute_dtype(*xs: Tensor) -> torch.dtype:
@@ -45,27 +48,44 @@ class BlockSparseFlashAttention(torch.autograd.Function):
         assert n % BlockSparseFlashAttention.FWD_BLOCK_M == 0, \
             "n must be a multiple of the 128-row query tile"
         out_dtype = q.dtype
-        cdt = _compute_dtype(q, k, v)
-        qc, kc, vc = q.to(cdt), k.to(cdt), v.to(cdt)
+        scaled = q.dtype == k.dtype == v.dtype == torch.float32
+        if scaled:
+            qc, kc, vc, a, c = _precision.qkv_to_f16(q, k, v)
+        else:
+            cdt = _compute_dtype(q, k, v)
+            qc, kc, vc = q.to(cdt), k.to(cdt), v.to(cdt)
         if torch.compiler.is_compiling():
             o, lse = torch.ops.bd3.attn_fwd(qc, kc, vc, int(block_size))
         else:
             o, lse = ops.attn_fwd_raw(qc, kc, vc, int(block_size))
-        ctx.save_for_backward(qc, kc, vc, o, lse)
+        ctx.scaled = scaled
+        ctx.save_for_backward(qc, kc, vc, o, lse, *((a, c) if scaled else ()))
         ctx.block_size = block_size
         ctx.out_dtypes = (q.dtype, k.dtype, v.dtype)
-        return o if out_dtype == cdt else o.to(out_dtype)
+        if scaled:
+            return _precision.scaled_back(o, c)
+        return o if out_dtype == o.dtype else o.to(out_dtype)
 
     @staticmethod
     def backward(ctx: Any, dO: Tensor):  # type: ignore[override]
-        q, k, v, O, L = ctx.saved_tensors
+        q, k, v, O, L = ctx.saved_tensors[:5]
         block_size = ctx.block_size
         n = q.shape[2] // 2
         assert n % block_size == 0
-        dO = dO.to(q.dtype)
+        if ctx.scaled:
+            a, c = ctx.saved_tensors[5:]
+            dO, e = _precision.grad_to_f16(dO)
+        else:
+            dO = dO.to(q.dtype)
         if torch.compiler.is_compiling():
             dq, dk, dv = torch.ops.bd3.attn_bwd(q, k, v, O, L, dO, int(block_size))
         else:
             dq, dk, dv = ops.attn_bwd_raw(q, k, v, O, L, dO, int(block_size))
+        if ctx.scaled:
+            # the kernel got 2^-e dO = 2^-(c+e) * (2^c dO), and 2^c dO is the cotangent of
+            # O' = 2^-c O, so its gradients are 2^-(c+e) times those of q', k', v'
+            d = c + e
+            return (_precision.scaled_back(dq, d - a), _precision.scaled_back(dk, d + a),
+                    _precision.scaled_back(dv, e), None)
         tq, tk, tv = ctx.out_dtypes
         return dq.to(tq), dk.to(tk), dv.to(tv), None

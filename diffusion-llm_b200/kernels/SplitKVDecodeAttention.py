@@ -8,12 +8,10 @@ per shape by the library's planner (bd3_decode_plan) instead of the fixed SPLIT_
 constant is kept for callers that read it.
 """
 
-import torch
 from torch import Tensor
 
-from bd3attn import ops
 from kernels.BlockSparseDecodeAttention import (  # noqa: F401
-    _cdt, _last_stride_1, block_sparse_decode_attention,
+    _cdt, _decode, _last_stride_1, block_sparse_decode_attention,
 )
 
 # keys per split of the reference (kernels/SplitKVDecodeAttention.py:13); informational here
@@ -31,11 +29,4 @@ def split_kv_decode_attention(
     if q_len > 64:
         # prefill: many query tiles already fill the GPU
         return block_sparse_decode_attention(q, k, v, block_size)
-    out_dtype = q.dtype
-    cdt = _cdt(q, k, v)
-    q, k, v = _last_stride_1(q.to(cdt)), _last_stride_1(k.to(cdt)), _last_stride_1(v.to(cdt))
-    if torch.compiler.is_compiling():
-        o = torch.ops.bd3.decode(q, k, v, int(block_size))
-    else:
-        o = ops.decode_raw(q, k, v, int(block_size))
-    return o if o.dtype == out_dtype else o.to(out_dtype)
+    return _decode(q, k, v, block_size)

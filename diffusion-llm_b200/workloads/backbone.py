@@ -11,7 +11,9 @@ The DiT's adaLN conditioning is left out (the reference runs with sigma = 0); it
 attention shape. The loss is the cross-entropy of the x_t half's logits against x_0 at the
 masked positions.
 
-``install_attention(name, block_size=bs, modules=ATTENTION)`` routes the layers.
+``use_attention(name, block_size)`` routes the layers. (The reference's own registry,
+bench/attention.py, patches its model.modules instead; bound to this repository's
+``kernels`` package it drives the reference's DiT the same way.)
 """
 
 from __future__ import annotations
@@ -22,8 +24,41 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-# the call site the layers look the attention function up on (patched by install_attention)
+# the call site the layers look the attention function up on (set by use_attention)
 ATTENTION = types.SimpleNamespace(scaled_dot_product_attention=None)
+
+# implementations use_attention can route to; the first three are this library's kernels
+# (through the drop-in kernels package) and take the block size, "sdpa" is PyTorch's
+# attention with the boolean mask as attn_mask, for comparison
+ROUTES = ("bsfa", "bsdfa", "split_kv", "sdpa")
+
+
+def use_attention(name: str, block_size: int | None = None) -> None:
+    """Point every layer's attention call (q, k, v, mask) at one implementation.
+
+    "bsfa": BlockSparseFlashAttention on the 2n training input (the mask argument is
+    implied by block_size); "bsdfa": block-causal attention of the last q_len positions
+    (prefill; with block_size equal to the length, plain bidirectional attention);
+    "split_kv": the same with the keys split for short query blocks; "sdpa": PyTorch's
+    attention given the mask. ValueError for an unknown name or a missing block size.
+    """
+    if name not in ROUTES:
+        raise ValueError(f"unknown attention route {name!r}; expected one of {ROUTES}")
+    if name == "sdpa":
+        ATTENTION.scaled_dot_product_attention = (
+            lambda q, k, v, mask: F.scaled_dot_product_attention(q, k, v, attn_mask=mask))
+        return
+    if block_size is None or block_size <= 0:
+        raise ValueError(f"route {name!r} needs a positive block_size")
+    if name == "bsfa":
+        from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
+        fn = BlockSparseFlashAttention.apply
+    elif name == "bsdfa":
+        from kernels.BlockSparseDecodeAttention import block_sparse_decode_attention as fn
+    else:
+        from kernels.SplitKVDecodeAttention import split_kv_decode_attention as fn
+    bs = int(block_size)
+    ATTENTION.scaled_dot_product_attention = lambda q, k, v, mask: fn(q, k, v, bs)
 
 
 def block_diff_mask(n: int, block_size: int, device=None) -> torch.Tensor:

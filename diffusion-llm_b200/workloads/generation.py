@@ -16,7 +16,7 @@ ops, a cache that concatenates (model/kv_cache.py:42-55, model/modules.py:410-41
 weights and Gumbel-max (sample/sampler.py:11-34, 114-122), and a commit that runs the whole
 backbone with store=True (model/bd3lm.py:210-233).
 
-Both take a ``Backbone`` (bench/backbone.py) in bf16; tokens/s = batch * length / time.
+Both take a ``Backbone`` (workloads/backbone.py) in bf16; tokens/s = batch * length / time.
 """
 
 from __future__ import annotations
@@ -26,7 +26,7 @@ import torch.nn.functional as F
 
 from bd3attn import ops
 from bd3attn.sampler import subs_sample_step_dev
-from bench.backbone import Backbone, rope, rope_tables
+from workloads.backbone import Backbone, rope, rope_tables, use_attention
 
 EPS = 1e-10
 NEG_INF = -1e6
@@ -210,11 +210,8 @@ class MDLMGeneration:
 
     @torch.no_grad()
     def run(self) -> torch.Tensor:
-        from bench import attention as ba
-        from bench import backbone as bb
         from bd3attn.sampler import subs_sample_step
-        ba.install_attention("bsdfa" if self.use_library else "sdpa", block_size=self.L,
-                             modules=bb.ATTENTION)
+        use_attention("bsdfa" if self.use_library else "sdpa", block_size=self.L)
         mask_index = self.m.mask_index
         dev = self.cos.device
         x = torch.full((self.B, self.L), mask_index, dtype=torch.int64, device=dev)

@@ -10,7 +10,7 @@
 // Outputs are fp32: S 128 x 128, O 128 x 64, C 128 x 64.
 #include <cstdint>
 
-#include "common.cuh"
+#include "../../diffusion-llm_b200/csrc/common.cuh"
 
 namespace {
 

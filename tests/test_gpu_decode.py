@@ -217,3 +217,19 @@ def test_full_config3_size():
     assert_device_ok()
     assert_close("O merged vs planned", merged, full, 1e-3)
     assert_close("LSE merged vs planned", merged_lse, full_lse, 1e-4)
+
+
+@pytest.mark.parametrize("q_len,kv_len", [(16, 1040), (16, 4112), (128, 640)])
+def test_fp32_decode_at_tf32_precision(q_len, kv_len):
+    """fp32 decode inputs (split-KV for a 16-token block, the tcgen05 prefill kernel for 128
+    queries) run on the fp16 kernels after the exact power-of-two scaling and return fp32 at
+    tf32-level error (11-bit operand significands)."""
+    from kernels.BlockSparseDecodeAttention import block_sparse_decode_attention
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    q, k, v = qkv(70 + q_len, 2, 12, q_len, kv_len, torch.float32)
+    ref, _ = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, 16))
+    for fn in (split_kv_decode_attention, block_sparse_decode_attention):
+        o = fn(q.cuda(), k.cuda(), v.cuda(), 16)
+        assert_device_ok()
+        assert o.dtype == torch.float32
+        assert_close(fn.__name__, o, ref, 2e-3)

@@ -1,4 +1,4 @@
-"""BD3-LM generation on the library (bench/generation.py) with a small stand-in backbone:
+"""BD3-LM generation on the library (workloads/generation.py) with a small stand-in backbone:
 one CUDA graph replay per block gives the same tokens as the same loop run eagerly; every
 generated token is a real token; and the cached forward over the committed blocks gives the
 logits of a full re-encode of the sequence under the block-causal mask (the reference's
@@ -17,13 +17,13 @@ CFG = dict(d_model=128, n_heads=2, n_layers=2, d_ff=256)
 
 @pytest.fixture(scope="module")
 def model():
-    from bench.backbone import Backbone
+    from workloads.backbone import Backbone
     torch.manual_seed(0)
     return Backbone(V, BS * N_BLOCKS, BS, **CFG).cuda().bfloat16().eval()
 
 
 def test_graph_replay_equals_eager_and_tokens_are_real(model):
-    from bench.generation import CachedGeneration
+    from workloads.generation import CachedGeneration
     got = CachedGeneration(model, B, N_BLOCKS, STEPS, seed=7).run().clone()
     again = CachedGeneration(model, B, N_BLOCKS, STEPS, seed=7, use_graph=False).run()
     assert_device_ok()
@@ -35,10 +35,9 @@ def test_graph_replay_equals_eager_and_tokens_are_real(model):
 
 
 def test_cached_forward_matches_full_reencode(model):
-    from bench import attention as ba
-    from bench import backbone as bb
-    from bench.generation import CachedGeneration
-    ba.install_attention("sdpa", modules=bb.ATTENTION)
+    from workloads import backbone as bb
+    from workloads.generation import CachedGeneration
+    bb.use_attention("sdpa")
     gen = CachedGeneration(model, B, N_BLOCKS, STEPS, seed=3, use_graph=False)
     tokens = gen.run().clone()
     gen._reset()  # teacher-forced pass over the generated tokens
@@ -58,7 +57,7 @@ def test_cached_forward_matches_full_reencode(model):
 
 
 def test_reference_flow_runs(model):
-    from bench.generation import ReferenceGeneration
+    from workloads.generation import ReferenceGeneration
     out = ReferenceGeneration(model, B, 2, STEPS, generator=torch.Generator(device="cuda").manual_seed(1)).run()
     assert out.shape == (B, 2 * BS) and bool(((out >= 0) & (out < V - 1)).all())
 
@@ -67,9 +66,8 @@ def test_mdlm_variant(model):
     """The MDLM loop (whole-sequence block, no cache): with the library's prefill attention
     the per-step logits equal PyTorch attention's within bf16 tolerance, and every token is
     unmasked at the end."""
-    from bench import attention as ba
-    from bench import backbone as bb
-    from bench.generation import MDLMGeneration
+    from workloads import backbone as bb
+    from workloads.generation import MDLMGeneration
     L = 128
     out = MDLMGeneration(model, 2, L, steps=8, seed=5).run()
     assert_device_ok()
@@ -78,9 +76,9 @@ def test_mdlm_variant(model):
     x[:, ::3] = V - 1  # a partly masked sequence
     gen = MDLMGeneration(model, 2, L, steps=1)
     with torch.no_grad():
-        ba.install_attention("bsdfa", block_size=L, modules=bb.ATTENTION)
+        bb.use_attention("bsdfa", block_size=L)
         ours = model.encode(x, None, gen.cos, gen.sin).float()
-        ba.install_attention("sdpa", modules=bb.ATTENTION)
+        bb.use_attention("sdpa")
         ref = model.encode(x, None, gen.cos, gen.sin).float()
     err = (ours - ref).abs().max().item()
     assert err <= 0.03 * max(1.0, ref.abs().max().item()), err

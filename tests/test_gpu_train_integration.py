@@ -18,20 +18,19 @@ CFG = dict(d_model=128, n_heads=2, n_layers=2, d_ff=512)
 
 
 def _models():
-    from bench.backbone import Backbone
+    from workloads.backbone import Backbone
     torch.manual_seed(0)
     a = Backbone(V, N, BS, **CFG).cuda()
     return a, copy.deepcopy(a)
 
 
 def _use(name):
-    from bench import attention as ba
-    from bench import backbone as bb
-    ba.install_attention(name, block_size=BS, modules=bb.ATTENTION)
+    from workloads import backbone as bb
+    bb.use_attention(name, block_size=BS)
 
 
 def test_first_step_gradients_agree():
-    from bench.backbone import noisy_batch
+    from workloads.backbone import noisy_batch
     ours, ref = _models()
     xt, x0 = (t.cuda() for t in noisy_batch(torch.Generator().manual_seed(1), BATCH, N, BS, V,
                                               repeat_blocks=True, n_tokens=64))
@@ -50,7 +49,7 @@ def test_first_step_gradients_agree():
 
 
 def test_loss_curves_agree_over_training():
-    from bench.backbone import noisy_batch, train_step
+    from workloads.backbone import noisy_batch, train_step
     ours, ref = _models()
     gen = torch.Generator().manual_seed(2)
     batches = [tuple(t.cuda() for t in noisy_batch(gen, BATCH, N, BS, V, repeat_blocks=True,

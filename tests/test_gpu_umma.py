@@ -7,7 +7,7 @@ import os
 import pytest
 import torch
 
-from conftest import PKG_ROOT
+from conftest import REPO
 from gpu_util import assert_device_ok
 
 pytestmark = pytest.mark.gpu
@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture(scope="module")
 def diag():
-    lib = ctypes.CDLL(os.path.join(PKG_ROOT, "lib", "libbd3diag.so"))
+    lib = ctypes.CDLL(os.path.join(REPO, "tests", "diag", "libbd3diag.so"))
     fn = lib.bd3diag_umma_selftest
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 9
@@ -46,7 +46,7 @@ def test_exp2_fma2_error_bound():
     """The forward's FMA-pipe exponential: relative error at most 1e-4 against exp2 over the
     softmax's argument range, exact +0 at and below -127 (and for -inf, the masked entries),
     within the same bound of the MUFU ex2.approx it stands in for."""
-    lib = ctypes.CDLL(os.path.join(PKG_ROOT, "lib", "libbd3diag.so"))
+    lib = ctypes.CDLL(os.path.join(REPO, "tests", "diag", "libbd3diag.so"))
     fn = lib.bd3diag_exp2
     fn.restype = ctypes.c_int
     fn.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
