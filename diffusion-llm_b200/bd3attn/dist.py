@@ -15,10 +15,17 @@ The reference is single-GPU; these are the two partitions the B200 build adds:
 ``sharded_decode`` takes the local-partial and merge functions as arguments so the same
 partition logic runs on CPU ranks (gloo) in the tests with a checker in their place; on the
 GPU the defaults are the library's kernels and there is no fallback.
+
+Failure detection between steps (``PeerWatch``): before a step's first launch, every rank
+posts that it reached the step in the process group's key-value store and waits, with a short
+limit, for every peer's post. A rank that left between steps is named on the survivors
+(``RankDropped``) before any of them launches a kernel or a collective of that step, so no
+GPU is left waiting inside a collective for a peer that will never arrive.
 """
 
 from __future__ import annotations
 
+import datetime
 from typing import Callable
 
 import torch
@@ -88,3 +95,41 @@ def sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor
     parts = gathered[..., : q_len * D].reshape(world, B, H, q_len, D)
     lses = gathered[..., q_len * D:].reshape(world, B, H, q_len)
     return merge_fn(parts.contiguous(), lses.contiguous(), out_dtype)
+
+
+class RankDropped(RuntimeError):
+    """Peers did not reach a step within the watch's limit; ``missing`` lists their ranks."""
+
+    def __init__(self, step: int, missing: list[int]):
+        super().__init__(f"ranks {missing} did not reach step {step}")
+        self.step = step
+        self.missing = missing
+
+
+class PeerWatch:
+    """Host-side liveness check of the ranks of one job, run between steps.
+
+    ``enter(step)`` sets the key ``<prefix>/<step>/<rank>`` in ``store`` (any
+    torch.distributed Store: the TCPStore or FileStore of the process group) and waits up to
+    ``timeout_s`` seconds for the same key of every rank. It raises RankDropped naming the
+    ranks whose key is missing. Keys of finished steps are not deleted (a step index is never
+    reused within a prefix).
+    """
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 2.0,
+                 prefix: str = "bd3/step"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout = datetime.timedelta(seconds=timeout_s)
+        self.prefix = prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def enter(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), "1")
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, self.timeout)
+        except Exception:  # the store's own timeout error; name who is missing
+            missing = [r for r in range(self.world) if not self.store.check([keys[r]])]
+            raise RankDropped(step, missing) from None

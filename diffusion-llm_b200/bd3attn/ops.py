@@ -195,6 +195,19 @@ def lse_merge_raw(parts, lses, out_dtype=torch.bfloat16):
     return o, lse
 
 
+def debug_wait_timeout(limit_ns: int, arrive: bool = False, device=None) -> tuple[int, int]:
+    """Run the bounded-wait self-check (bd3_debug_wait_timeout) on the current stream and
+    return (1 if the wait gave up else 0, the wait's duration in ns). Synchronises."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    out = torch.zeros(2, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        check("bd3_debug_wait_timeout", LIB.bd3_debug_wait_timeout(
+            int(limit_ns), 1 if arrive else 0, _ptr(out),
+            ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)))
+    res = out.cpu()
+    return int(res[0]), int(res[1])
+
+
 def device_status(clear: bool = True) -> int:
     """Sticky device-side error bits (1: a bounded wait ran out; 2: a kernel rejected its
     launch; 4: a RoPE position was outside the table). Synchronises."""

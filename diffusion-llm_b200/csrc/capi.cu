@@ -994,6 +994,17 @@ int bd3_debug_ranges(int kind, int64_t start, int64_t tile_a, int64_t tile_b, in
   return cnt;
 }
 
+int bd3_debug_wait_timeout(int64_t limit_ns, int arrive, uint64_t* out, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000)
+    return fail(BD3_ERR_INVALID, "limit_ns must be in [1e3, 1e9] (got %lld)", (long long)limit_ns);
+  if (out == nullptr || reinterpret_cast<uintptr_t>(out) % 8)
+    return fail(BD3_ERR_INVALID, "out must be an 8-byte aligned device buffer of 2 uint64");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  bd3::wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<unsigned long long>(limit_ns), arrive, reinterpret_cast<unsigned long long*>(out));
+  return check_launch("wait_probe_kernel launch");
+}
+
 int bd3_debug_tiles(int32_t* out) {
   out[0] = bd3::kFwdBM;
   out[1] = bd3::kFwdBN;

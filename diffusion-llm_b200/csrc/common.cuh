@@ -85,17 +85,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Wait for the phase of the given parity to complete. Bounded: returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// Wait for the phase of the given parity to complete. Bounded: returns false when limit_ns
+// nanoseconds pass first (kWaitNs in the kernels; the self-check below passes a short one).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned long long limit_ns = kWaitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023u) == 0 && globaltimer_ns() - t0 > kWaitNs) {
+    if ((i & 1023u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       atomicOr(&g_bd3_status, kStatusWaitTimeout);
       return false;
     }
   }
+}
+
+// Self-check of the bounded wait (bd3_debug_wait_timeout): thread 0 initialises an mbarrier
+// expecting one arrival, arrives on it only when `arrive` is set, and waits for its first
+// phase with the given limit. With no arrival nothing can complete the phase, so the wait
+// must give up after limit_ns, set kStatusWaitTimeout and return; the kernel then exits
+// normally. out[0] = 1 when the wait gave up, 0 when the phase completed; out[1] = the
+// nanoseconds the wait took.
+__global__ void wait_probe_kernel(unsigned long long limit_ns, int arrive,
+                                  unsigned long long* out) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  fence_mbar_init();
+  if (arrive) mbar_arrive(&bar);
+  const unsigned long long t0 = globaltimer_ns();
+  const bool ok = mbar_wait(&bar, 0, limit_ns);
+  out[1] = globaltimer_ns() - t0;
+  out[0] = ok ? 0ull : 1ull;
 }
 
 // Warp-uniform wait for warps that go on to issue warp-collective (.sync.aligned)

@@ -22,6 +22,11 @@ from bd3attn import ops
 from kernels import _precision
 
 
+# query-tile height of the sm_100a training kernels; n must be a multiple of it (a module
+# constant: torch.compile cannot read attributes of the autograd.Function class while tracing)
+_FWD_TILE_M = 128
+
+
 def _compute_dtype(*xs: Tensor) -> torch.dtype:
     dts = {x.dtype for x in xs}
     if dts <= {torch.float16}:
@@ -34,7 +39,7 @@ class BlockSparseFlashAttention(torch.autograd.Function):
 
     # tile shape of the sm_100a kernels (the reference's Triton tiles were 128x64 forward,
     # 128x64 dQ and 128x32 dK/dV); the same range formulas select the visited tiles
-    FWD_BLOCK_M, FWD_BLOCK_N = 128, 128
+    FWD_BLOCK_M, FWD_BLOCK_N = _FWD_TILE_M, 128
     BWD_DQ_BLOCK_M, BWD_DQ_BLOCK_N = 128, 128
     BWD_DKDV_BLOCK_KV, BWD_DKDV_BLOCK_Q = 128, 128
 
@@ -45,8 +50,7 @@ class BlockSparseFlashAttention(torch.autograd.Function):
         assert q.shape == k.shape == v.shape, "q, k, v must match"
         assert seq_len % 2 == 0, "BD3-LM input is cat(x_t, x_0): length 2n"
         n = seq_len // 2
-        assert n % BlockSparseFlashAttention.FWD_BLOCK_M == 0, \
-            "n must be a multiple of the 128-row query tile"
+        assert n % _FWD_TILE_M == 0, "n must be a multiple of the 128-row query tile"
         out_dtype = q.dtype
         scaled = q.dtype == k.dtype == v.dtype == torch.float32
         if scaled:

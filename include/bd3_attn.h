@@ -242,6 +242,17 @@ BD3_API int bd3_debug_ranges(int kind, int64_t start, int64_t tile_a, int64_t ti
                      int64_t kv_len, int64_t block_size, int32_t* out);
 BD3_API int bd3_debug_tiles(int32_t* out);
 
+/* Self-check of the kernels' bounded waits (tests; no counterpart in the reference, which
+ * has no device-side failure handling). One thread initialises an mbarrier expecting one
+ * arrival, arrives on it only when `arrive` is non-zero, and waits for it with the limit
+ * `limit_ns` (1e3 .. 1e9, else BD3_ERR_INVALID) through the same wait every kernel uses.
+ * Without the arrival the wait must give up after limit_ns: the kernel sets status bit 1
+ * (read and cleared by bd3_device_status) and exits normally, leaving the context usable.
+ * out: a device buffer of 2 uint64, written with (1 if the wait gave up else 0, the wait's
+ * duration in ns). Enqueued on `stream`.
+ */
+BD3_API int bd3_debug_wait_timeout(int64_t limit_ns, int arrive, uint64_t* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -103,3 +103,12 @@ def test_capi_devlen_decode_argument_checks():
     assert _devlen(q_len=0) == BD3_ERR_UNSUPPORTED
     assert _devlen(cap=8) == BD3_ERR_INVALID       # capacity below the query block
     assert _devlen(out_dtype=1) == BD3_ERR_INVALID  # bf16 in, fp16 out
+
+
+def test_wait_self_check_rejects_bad_limits_on_the_host():
+    """bd3_debug_wait_timeout validates its arguments before touching the GPU."""
+    from bd3attn._lib import BD3_ERR_INVALID, LIB
+    assert LIB.bd3_debug_wait_timeout(10, 0, None, None) == BD3_ERR_INVALID
+    assert LIB.bd3_debug_wait_timeout(2 * 10 ** 9, 0, None, None) == BD3_ERR_INVALID
+    assert b"limit_ns" in LIB.bd3_last_error()
+    assert LIB.bd3_debug_wait_timeout(10 ** 6, 0, None, None) == BD3_ERR_INVALID  # no buffer

@@ -92,3 +92,69 @@ def test_sharded_decode_equals_full_attention(tmp_path, world, kv_len, q_len, bs
     ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, kv_len, bs))
     torch.testing.assert_close(o, ref, atol=1e-5, rtol=1e-5)
     torch.testing.assert_close(lse.double(), ref_lse, atol=1e-5, rtol=1e-5)
+
+
+def _dropout_worker(rank, world, port, leave_rank, leave_after, mode, out_dir):
+    """Steps of sequence-sharded decode on gloo ranks; ``leave_rank`` returns after finishing
+    step ``leave_after`` (between steps: none of its collectives in flight). mode "watch":
+    the survivors check their peers in the store before each step; mode "collective": they
+    do not, and the process group's short timeout ends the next collective with an error."""
+    import datetime
+    import json
+
+    from bd3attn.dist import PeerWatch, RankDropped
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=30))
+    dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    watch = PeerWatch(store, rank, world, timeout_s=2.0)
+    g = torch.Generator().manual_seed(0)
+    q = torch.randn(1, 2, 16, 64, generator=g)
+    k = torch.randn(1, 2, 320, 64, generator=g)
+    v = torch.randn(1, 2, 320, 64, generator=g)
+    a, b = seq_shard(320, world, rank)
+    record = {"rank": rank, "steps_done": [], "error": None}
+    try:
+        for step in range(4):
+            if mode == "watch":
+                watch.enter(step)
+            o, _ = sharded_decode(q, k[:, :, a:b], v[:, :, a:b], 16, a, 320,
+                                  out_dtype=torch.float64, partial_fn=_oracle_partial,
+                                  merge_fn=_oracle_merge)
+            record["steps_done"].append(step)
+            record["o_sum"] = float(o.sum())
+            if rank == leave_rank and step == leave_after:
+                record["left"] = True
+                break
+    except RankDropped as e:
+        record["error"] = {"kind": "RankDropped", "step": e.step, "missing": e.missing}
+    except RuntimeError as e:  # the collective's timeout
+        record["error"] = {"kind": "collective", "message": str(e)[:200]}
+    with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
+        json.dump(record, f)
+    if rank == 0 and mode == "watch":
+        # the store's server lives in rank 0: keep it up until the peers have read it
+        import time
+        time.sleep(0.5)
+
+
+@pytest.mark.parametrize("mode", ["watch", "collective"])
+def test_rank_dropout_between_steps(tmp_path, mode):
+    """world_size 3: rank 2 leaves after step 1. The survivors finish steps 0 and 1 with the
+    right result and then end with an error instead of waiting: with the store watch they
+    name rank 2 as missing at step 2 before launching anything of that step; without it the
+    process group's 3 s timeout ends their step-2 all-gather."""
+    import json
+    world = 3
+    mp.spawn(_dropout_worker, args=(world, _free_port(), 2, 1, mode, str(tmp_path)),
+             nprocs=world, join=True)
+    recs = [json.load(open(tmp_path / f"rank{r}.json")) for r in range(world)]
+    assert recs[2].get("left") and recs[2]["steps_done"] == [0, 1] and recs[2]["error"] is None
+    sums = {r["o_sum"] for r in recs}
+    assert len(sums) == 1  # every rank merged the same result before the dropout
+    for r in recs[:2]:
+        assert r["steps_done"] == [0, 1], r
+        if mode == "watch":
+            assert r["error"] == {"kind": "RankDropped", "step": 2, "missing": [2]}, r
+        else:
+            assert r["error"]["kind"] == "collective", r

@@ -135,7 +135,7 @@ def test_fp32_inputs_config1():
 
 
 def test_fp32_inputs_wide_range_and_backward():
-    """fp32 inputs far outside fp16's range (q x 2^20, k x 2^-18, v x 2^30) give the same
+    """fp32 inputs far outside fp16's range (q x 2^20, k x 2^-20, v x 2^30) give the same
     results as unscaled ones up to the power-of-two factors: the scaling into fp16 is exact.
     The backward's dQ, dK, dV come back in fp32 at tf32-level error."""
     from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
@@ -153,20 +153,17 @@ def test_fp32_inputs_wide_range_and_backward():
     assert_close("O", o, ref_o, F32_O_TOL)
     for name, got, ref in (("dQ", dq, rdq), ("dK", dk, rdk), ("dV", dv, rdv)):
         assert_close(name, got, ref, F32_GRAD_TOL)
-    sq, sk, sv = 2.0 ** 20, 2.0 ** -18, 2.0 ** 30
+    sq, sk, sv = 2.0 ** 20, 2.0 ** -20, 2.0 ** 30
     ys = [(t.detach() * s).requires_grad_(True) for t, s in zip(xs, (sq, sk, sv))]
     o2 = BlockSparseFlashAttention.apply(*ys, bs)
     dq2, dk2, dv2 = torch.autograd.grad(o2, ys, do.cuda() * 2.0 ** -7)
     assert_device_ok()
-    # q . k is 4x the original: compare with the oracle of the same scores, scaled back
-    ref_o2, _ = oracle.attention(q * 4.0, k, v, mask)
-    assert_close("O (wide range) / 2^30", o2 / sv, ref_o2, F32_O_TOL)
-    assert torch.isfinite(dq2).all() and torch.isfinite(dk2).all() and torch.isfinite(dv2).all()
-    rdq2, rdk2, rdv2 = oracle.attention_grads(q * 4.0, k, v, do, mask)
-    # O2 = 2^30 attn(2^-18 q2, k, v) and dO2 = 2^-7 dO: dV2 = 2^-7 dV and
-    # dQ2 = 2^30 * 2^-18 * 2^-7 dQ = 2^5 dQ, with dQ, dV the oracle's at (4q, k, v)
-    assert_close("dV (wide range)", dv2 * 2.0 ** 7, rdv2, F32_GRAD_TOL)
-    assert_close("dQ (wide range)", dq2 * 2.0 ** -5, rdq2, F32_GRAD_TOL)
+    # the scores q . k are unchanged: O2 = 2^30 O, and with dO2 = 2^-7 dO the gradients are
+    # dQ2 = 2^30 2^-20 2^-7 dQ, dK2 = 2^30 2^20 2^-7 dK, dV2 = 2^-7 dV
+    assert_close("O (wide range) / 2^30", o2 / sv, ref_o, F32_O_TOL)
+    assert_close("dQ (wide range)", dq2 * 2.0 ** -3, rdq, F32_GRAD_TOL)
+    assert_close("dK (wide range)", dk2 * 2.0 ** -43, rdk, F32_GRAD_TOL)
+    assert_close("dV (wide range)", dv2 * 2.0 ** 7, rdv, F32_GRAD_TOL)
 
 
 def test_reference_assertions():
