@@ -13,6 +13,7 @@
 #include "../../include/bd3_attn.h"
 #include "attn_bwd.cuh"
 #include "attn_fwd.cuh"
+#include "attn_fwd_pair.cuh"
 #include "decode.cuh"
 #include "kv_rope.cuh"
 #include "sampler.cuh"
@@ -243,21 +244,29 @@ int launch_fwd(int mode, const void* q, const void* k, const void* v, void* o, f
   if (items > 2147483647LL) return fail(BD3_ERR_UNSUPPORTED, "too many query tiles");
   int sms = 148;
   if ((rc = current_device_sms(&sms)) != BD3_OK) return rc;
-  const int64_t grid = items < sms ? items : sms;  // persistent: one CTA per SM
   void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap,
                const bd3::FwdParams);
   int slot;
   if (mode == bd3::kTrain) {
-    kern = dtype == BD3_BF16 ? bd3::attn_fwd_kernel<bd3::kTrain, true>
-                             : bd3::attn_fwd_kernel<bd3::kTrain, false>;
+    // items are (batch*head, tile pair): the noisy and clean query tiles i share K/V
+    const int64_t pairs = B * H * (n / bd3::kFwdBM);
+    const int64_t grid = pairs < sms ? pairs : sms;  // persistent: one CTA per SM
+    kern = dtype == BD3_BF16 ? bd3::attn_fwd_pair_kernel<true> : bd3::attn_fwd_pair_kernel<false>;
     slot = dtype == BD3_BF16 ? 0 : 1;
-  } else {
+    if ((rc = set_smem(kern, bd3::PairSmem::kAlloc, slot)) != BD3_OK) return rc;
+    ProfScope ps(kPfFwd, stream);
+    kern<<<static_cast<unsigned>(grid), bd3::kPairThreads, bd3::PairSmem::kAlloc, stream>>>(
+        tq, tk, tv, to, p);
+    return check_launch("attn_fwd_pair_kernel launch");
+  }
+  const int64_t grid = items < sms ? items : sms;  // persistent: one CTA per SM
+  {
     kern = dtype == BD3_BF16 ? bd3::attn_fwd_kernel<bd3::kDecode, true>
                              : bd3::attn_fwd_kernel<bd3::kDecode, false>;
     slot = dtype == BD3_BF16 ? 2 : 3;
   }
   if ((rc = set_smem(kern, bd3::FwdSmem::kAlloc, slot)) != BD3_OK) return rc;
-  ProfScope ps(mode == bd3::kTrain ? kPfFwd : kPfPrefill, stream);
+  ProfScope ps(kPfPrefill, stream);
   kern<<<static_cast<unsigned>(grid), bd3::kFwdThreads, bd3::FwdSmem::kAlloc, stream>>>(tq, tk, tv, to, p);
   return check_launch("attn_fwd_kernel launch");
 }

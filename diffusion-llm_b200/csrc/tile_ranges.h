@@ -28,25 +28,38 @@ BD3_HD int imax(int a, int b) { return a > b ? a : b; }
 BD3_HD int cdiv(int a, int b) { return (a + b - 1) / b; }
 
 // Key ranges of the program over query rows [q_start, q_start + bm) of the 2n training
-// sequence. Returns the number of ranges written to out (3 for noisy tiles, 2 for clean).
-BD3_HD int fwd_ranges(int q_start, int bm, int bn, int n, int bs, Range* out) {
+// sequence, for a noisy program (q_start < n): rule 1 over its own noisy blocks, then rule 0
+// and rule 2 (shift 1) over the clean keys.
+BD3_HD void fwd_ranges_noisy(int q_start, int bm, int bn, int n, int bs, Range& a, Range& b,
+                             Range& c) {
   const int r0 = q_start, r1 = q_start + bm - 1;
-  int k = 0, full, hi, shift;
+  const int lo_a = ((r0 / bs) * bs / bn) * bn;
+  const int hi_a = imin((r1 / bs + 1) * bs, n);
+  a = Range{lo_a, hi_a, 1, 1};
+  const int full = n + ((r0 / bs) * bs / bn) * bn;
+  const int hi = n + (r1 / bs) * bs;
+  b = Range{n, full, 0, 1};
+  c = Range{full, hi, 2, 1};
+}
+
+// The same for a clean program (q_start >= n): rule 0, then rule 2 (shift 0).
+BD3_HD void fwd_ranges_clean(int q_start, int bm, int bn, int n, int bs, Range& b, Range& c) {
+  const int r0 = q_start, r1 = q_start + bm - 1;
+  const int full = n + ((((r0 - n) / bs + 1) * bs) / bn) * bn;
+  const int hi = imin(n + ((r1 - n) / bs + 1) * bs, 2 * n);
+  b = Range{n, full, 0, 0};
+  c = Range{full, hi, 2, 0};
+}
+
+// Both, as the reference's program computes them: returns the number of ranges written to
+// out (3 for noisy tiles, 2 for clean).
+BD3_HD int fwd_ranges(int q_start, int bm, int bn, int n, int bs, Range* out) {
   if (q_start < n) {
-    shift = 1;
-    const int lo_a = ((r0 / bs) * bs / bn) * bn;
-    const int hi_a = imin((r1 / bs + 1) * bs, n);
-    out[k++] = Range{lo_a, hi_a, 1, shift};
-    full = n + ((r0 / bs) * bs / bn) * bn;
-    hi = n + (r1 / bs) * bs;
-  } else {
-    shift = 0;
-    full = n + ((((r0 - n) / bs + 1) * bs) / bn) * bn;
-    hi = imin(n + ((r1 - n) / bs + 1) * bs, 2 * n);
+    fwd_ranges_noisy(q_start, bm, bn, n, bs, out[0], out[1], out[2]);
+    return 3;
   }
-  out[k++] = Range{n, full, 0, shift};
-  out[k++] = Range{full, hi, 2, shift};
-  return k;
+  fwd_ranges_clean(q_start, bm, bn, n, bs, out[0], out[1]);
+  return 2;
 }
 
 // Query ranges of the program over keys [k_start, k_start + bkv). Returns 1 or 4.

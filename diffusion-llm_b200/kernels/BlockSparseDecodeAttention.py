@@ -55,7 +55,9 @@ def _decode(q: Tensor, k: Tensor, v: Tensor, block_size: int) -> Tensor:
     else:
         cdt = _cdt(q, k, v)
         q, k, v, c, odt = q.to(cdt), k.to(cdt), v.to(cdt), None, None
-    q, k, v = _last_stride_1(q), _last_stride_1(k), _last_stride_1(v)
+    # forward only, as the reference's decode kernels: the output carries no autograd
+    # history (detached inputs keep torch.compile from asking for a backward formula)
+    q, k, v = _last_stride_1(q.detach()), _last_stride_1(k.detach()), _last_stride_1(v.detach())
     if torch.compiler.is_compiling():
         o = torch.ops.bd3.decode(q, k, v, int(block_size))
         if c is not None:

@@ -15,6 +15,7 @@ CASES = [  # (B, H, n, block_size)
     (1, 1, 256, 256), (1, 2, 1024, 16), (1, 1, 1024, 4), (1, 1, 384, 32), (1, 1, 512, 1024 // 2),
     (1, 1, 128, 1),      # one-token blocks: the densest rule pattern
     (1, 1, 2048, 64), (1, 1, 4096, 128),  # long sequences (2n = 4096, 8192)
+    (16, 12, 256, 16),   # 384 items on 148 persistent CTAs: several items per CTA
 ]
 
 
