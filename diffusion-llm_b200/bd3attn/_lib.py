@@ -56,6 +56,7 @@ SIGNATURES = {
     "bd3_debug_ranges": (_i32, [_i32, _i64, _i64, _i64, _i64, _i64, _i64, _pi32]),
     "bd3_debug_tiles": (_i32, [_pi32]),
     "bd3_debug_wait_timeout": (_i32, [_i64, _i32, _vp, _vp]),
+    "bd3_debug_wait_site": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),
 }
 
 

@@ -208,6 +208,17 @@ def debug_wait_timeout(limit_ns: int, arrive: bool = False, device=None) -> tupl
     return int(res[0]), int(res[1])
 
 
+def debug_wait_site() -> dict | None:
+    """Where the first bounded wait that ran out gave up since the last read (block, thread,
+    barrier shared-memory address, awaited parity), or None; reading clears it."""
+    out = (ctypes.c_uint32 * 4)()
+    check("bd3_debug_wait_site", LIB.bd3_debug_wait_site(out))
+    if not out[0]:
+        return None
+    return {"block": out[1], "thread": out[2], "smem_addr": out[3] & 0x7FFFFFFF,
+            "parity": out[3] >> 31}
+
+
 def device_status(clear: bool = True) -> int:
     """Sticky device-side error bits (1: a bounded wait ran out; 2: a kernel rejected its
     launch; 4: a RoPE position was outside the table). Synchronises."""

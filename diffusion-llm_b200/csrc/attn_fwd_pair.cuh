@@ -39,9 +39,9 @@ struct PairSmem {
   static constexpr uint32_t kV = kK + kPairStages * kTile16;
   static constexpr uint32_t kOut = kV + kPairStages * kTile16;    // [noisy, clean] O staging
   static constexpr uint32_t kBar = kOut + 2 * kTile16;
-  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[3], p_full[3],
+  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[2][3], p_full[3],
   // o_done[2], o_free[2]
-  static constexpr uint32_t kNumBars = 4 + 3 * kPairStages + 10;
+  static constexpr uint32_t kNumBars = 4 + 3 * kPairStages + 13;
   static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
   static constexpr uint32_t kBytes = kTmemSlot + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // room to align the base to 1 KB
@@ -131,10 +131,14 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* k_full = bars + 4;
   uint64_t* v_full = bars + 4 + kPairStages;
   uint64_t* kv_empty = bars + 4 + 2 * kPairStages;
-  uint64_t* s_full = bars + 4 + 3 * kPairStages;    // [S buffer]
-  uint64_t* p_full = s_full + 3;                    // [S buffer]
-  uint64_t* o_done = s_full + 6;                    // [noisy, clean]
-  uint64_t* o_free = s_full + 8;                    // [noisy, clean]
+  // s_full[x][b] completes when an S tile of query tile x has landed in buffer b: one
+  // barrier per warpgroup and buffer, so a warpgroup only ever waits for the next phase of
+  // its own barriers (a shared barrier per buffer could be two phases behind a warpgroup
+  // whose previous tile used another buffer, and a parity wait cannot tell those apart)
+  uint64_t* s_full = bars + 4 + 3 * kPairStages;    // [noisy, clean][S buffer]
+  uint64_t* p_full = s_full + 6;                    // [S buffer]
+  uint64_t* o_done = s_full + 9;                    // [noisy, clean]
+  uint64_t* o_free = s_full + 11;                   // [noisy, clean]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PairSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
@@ -155,6 +159,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int b = 0; b < 3; ++b) {
       mbar_init(&s_full[b], 1);
+      mbar_init(&s_full[3 + b], 1);
       mbar_init(&p_full[b], 128);
     }
     fence_mbar_init();
@@ -262,7 +267,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int kk = 0; kk < 4; ++kk)
               umma_ss(tmem + b * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
                       idesc_qk, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[b]);
+            umma_commit(&s_full[x * 3 + b]);
             if (j == steps - 1 && x == last_x) umma_commit(&q_empty[qb]);
             const Pv cur{t, x, it, J, first[x], x == last_x};
             first[x] = false;
@@ -295,6 +300,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     bool ok = true;
     int t = 0;   // S tiles of both warpgroups issued before the current one
     int pv = 0;  // P V products of this warpgroup's tile so far
+    uint32_t s_phase = 0;  // bit b: parity of the next phase of s_full[x][b] to wait for
     for (int it = 0, w = persistent_item(0); w < num_items; w = persistent_item(++it)) {
       int bh, i;
       pair_item(w, p.num_bh, num_pairs, &bh, &i);
@@ -313,8 +319,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
         const int b = t % 3;
         const int rule = ps.rule[x];
-        ok = mbar_wait_warp(&s_full[b], (t / 3) & 1);
+        ok = mbar_wait_warp(&s_full[x * 3 + b], (s_phase >> b) & 1u);
         if (!ok) break;
+        s_phase ^= 1u << b;
         tc_fence_after();
         const uint32_t tS = tmem + lane_base + b * 128;
         // this row's visible key columns of the tile, and which 32-column chunks any row of

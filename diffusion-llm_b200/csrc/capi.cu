@@ -1014,6 +1014,16 @@ int bd3_debug_wait_timeout(int64_t limit_ns, int arrive, uint64_t* out, void* st
   return check_launch("wait_probe_kernel launch");
 }
 
+int bd3_debug_wait_site(uint32_t* out) {
+  if (out == nullptr) return fail(BD3_ERR_INVALID, "out must hold 4 uint32");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  cudaError_t e = cudaMemcpyFromSymbol(out, bd3::g_bd3_wait_site, 4 * sizeof(uint32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "reading the wait site");
+  const uint32_t zero[4] = {0, 0, 0, 0};
+  e = cudaMemcpyToSymbol(bd3::g_bd3_wait_site, zero, sizeof(zero));
+  return e == cudaSuccess ? BD3_OK : cuda_fail(e, "clearing the wait site");
+}
+
 int bd3_debug_tiles(int32_t* out) {
   out[0] = bd3::kFwdBM;
   out[1] = bd3::kFwdBN;

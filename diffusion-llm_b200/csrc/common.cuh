@@ -27,6 +27,9 @@ enum : unsigned {
   kStatusBadLaunch = 2u,     // a kernel saw launch parameters it cannot handle
 };
 __device__ unsigned int g_bd3_status;
+// Where the first bounded wait that ran out gave up: [0] set flag, [1] block, [2] thread,
+// [3] the barrier's shared-memory address | parity << 31 (read by bd3_debug_wait_site).
+__device__ unsigned int g_bd3_wait_site[4];
 
 constexpr unsigned long long kWaitNs = 500000000ull;  // 0.5 s: far above any legitimate wait
 
@@ -95,6 +98,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023u) == 0 && globaltimer_ns() - t0 > limit_ns) {
       atomicOr(&g_bd3_status, kStatusWaitTimeout);
+      if (atomicCAS(&g_bd3_wait_site[0], 0u, 1u) == 0u) {
+        g_bd3_wait_site[1] = blockIdx.x;
+        g_bd3_wait_site[2] = threadIdx.x;
+        g_bd3_wait_site[3] = smem_u32(bar) | (parity << 31);
+      }
       return false;
     }
   }

@@ -253,6 +253,12 @@ BD3_API int bd3_debug_tiles(int32_t* out);
  */
 BD3_API int bd3_debug_wait_timeout(int64_t limit_ns, int arrive, uint64_t* out, void* stream);
 
+/* Where the first bounded wait that ran out since the last call gave up (no counterpart in
+ * the reference): out[0] 1 if one did (else all 0), out[1] its block, out[2] its thread,
+ * out[3] the barrier's shared-memory address with the awaited parity in bit 31. Reading
+ * clears it. Synchronous. */
+BD3_API int bd3_debug_wait_site(uint32_t* out);
+
 #ifdef __cplusplus
 }
 #endif

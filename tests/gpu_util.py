@@ -33,4 +33,5 @@ def assert_device_ok():
     from bd3attn import ops
     torch.cuda.synchronize()
     st = ops.device_status(clear=True)
-    assert st == 0, f"device status bits {st} (a bounded wait ran out)"
+    site = ops.debug_wait_site()
+    assert st == 0, f"device status bits {st} (a bounded wait ran out: {site})"

@@ -19,6 +19,9 @@ def test_bounded_wait_gives_up_and_context_stays_usable():
     assert 1_000_000 <= ns < 100_000_000, ns
     assert ops.device_status(clear=True) == 1  # bit 1: a bounded wait ran out
     assert ops.device_status(clear=True) == 0  # and reading it cleared it
+    site = ops.debug_wait_site()  # the probe's one waiting thread, parity 0
+    assert site is not None and site["block"] == 0 and site["thread"] == 0 and site["parity"] == 0
+    assert ops.debug_wait_site() is None  # reading it cleared it
     # control: with the arrival the same wait completes at once and records nothing
     gave_up, ns = ops.debug_wait_timeout(1_000_000, arrive=True)
     assert gave_up == 0 and ns < 1_000_000
@@ -37,6 +40,7 @@ def test_repeated_timeouts_stay_sticky_until_read():
     for _ in range(3):
         assert ops.debug_wait_timeout(20_000)[0] == 1
     torch.cuda.synchronize()
+    assert ops.debug_wait_site() is not None
     assert ops.device_status(clear=False) == 1  # read without clearing: still set
     assert ops.device_status(clear=True) == 1
     assert ops.device_status(clear=True) == 0
