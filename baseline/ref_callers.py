@@ -1,9 +1,9 @@
 """The reference's own callers, unchanged, run against this repository's ``kernels`` package.
 
-Run as a subprocess by tests/test_reference_callers.py (and by bench.py's reference-training
-row), one case per call:
+Run as a subprocess by tests/test_reference_callers.py and by bench.py (the reference's
+training loop on both attention backends), one case per call:
 
-    python tests/ref_callers.py <case> [json arguments]
+    python baseline/ref_callers.py <case> [json arguments]
 
 The import path is this repository's package root (``kernels``, ``bd3attn``) followed by the
 installed reference (baseline/_ref: ``model``, ``bench``, ``sample``, ``inference``,
@@ -32,7 +32,7 @@ import tempfile
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
 PKG = os.path.join(REPO, "diffusion-llm_b200")
-REF = os.path.join(REPO, "baseline", "_ref")
+REF = os.path.join(HERE, "_ref")
 
 # this package first, then the installed reference; nothing else from the repository root
 # (its bench.py would shadow the reference's bench package)

@@ -742,6 +742,43 @@ def sampler_extras(dev, l2, peaks, reps: int = 10) -> dict:
                                      "frac_hbm": round(by / ours / 1e6 / peaks["hbm_gbs"], 4)}}
 
 
+def run_json_script(argv: list[str], timeout: int = 900) -> dict:
+    """Run a helper under baseline/ in a child process and return its last JSON line, or
+    {"unavailable": <why>} when it cannot run (the reference not installed, a failure)."""
+    import subprocess
+    try:
+        r = subprocess.run([sys.executable, *argv], capture_output=True, text=True,
+                           timeout=timeout, cwd=REPO)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"{argv[0]} did not finish within {timeout} s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"unavailable": f"{argv[0]} exited {r.returncode}: {tail[0][:300]}"}
+    return json.loads(lines[-1])
+
+
+def reference_extras() -> dict:
+    """The reference itself on this GPU (installed unchanged in baseline/_ref): its Triton
+    kernels timed at configs 2 and 3 (baseline/triton_reference.py), and its training loop
+    (train/train.py main: BD3LM at the "small" config, batch 16, n = 1024, bf16 autocast,
+    AdamW) with --attn bsfa (this library through the drop-in kernels package) and --attn
+    custom (the reference's own masked attention), tokens/s as train.py reports them."""
+    out = {"triton_kernels": run_json_script([os.path.join("baseline", "triton_reference.py")])}
+    cfg = {"seq_len": 1024, "batch_size": 16, "d_model": 768, "n_heads": 12, "n_layers": 12,
+           "d_ff": 3072, "d_cond": 128, "steps": 12, "warmup_steps": 4}
+    loop = run_json_script([os.path.join("baseline", "ref_callers.py"), "train_loop",
+                            json.dumps(cfg)])
+    if "unavailable" not in loop:
+        loop = {"bsfa_tokens_per_s": round(loop["bsfa"]["tokens_per_s"]),
+                "custom_tokens_per_s": round(loop["custom"]["tokens_per_s"]),
+                "speedup": round(loop["bsfa"]["tokens_per_s"] / loop["custom"]["tokens_per_s"], 3),
+                "loss_max_rel_diff": round(loop["loss_max_rel_diff"], 5),
+                "config": loop["config"]}
+    out["train_loop"] = loop
+    return out
+
+
 def run_ours(args) -> None:
     world, rank, local = dist_setup(args.gpus)
     from bd3attn import ops
@@ -938,6 +975,7 @@ def run_ours(args) -> None:
             extra["graph_step"] = graph_step_extras(dev, l2, peaks)
             extra["train_step"] = train_step_extras(dev, l2, peaks)
             extra["mdlm"] = mdlm_extras(dev, l2, peaks)
+            extra["reference"] = reference_extras()
     cpu = cpu_baseline() if (rank == 0 and world == 1 and not args.no_cpu) else None
     if rank == 0:
         line = {
@@ -1000,7 +1038,7 @@ def main():
                          "the command the decode ncu captures run")
     ap.add_argument("--extra", choices=("kv_cache", "sampler", "live_decode", "graph_step",
                                         "train_step", "generation", "mdlm", "sharded_decode",
-                                        "decode_grid", "c1"),
+                                        "decode_grid", "c1", "reference"),
                     help="time only that extra measurement (the command its ncu capture runs)")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -1020,6 +1058,8 @@ def main():
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
+    elif args.extra == "reference":
+        print(json.dumps(reference_extras()), flush=True)
     elif args.extra:
         torch.cuda.set_device(0)
         dev = torch.device("cuda", 0)

@@ -1,6 +1,6 @@
 """The reference's callers, unchanged, drive this repository's kernels (the drop-in claim).
 
-Each case runs tests/ref_callers.py in a fresh process whose import path holds this
+Each case runs baseline/ref_callers.py in a fresh process whose import path holds this
 package and the reference installed by baseline/install_reference.py (baseline/_ref), so the
 reference's bench/attention.py, model/bd3lm.py, sample/sampler.py, inference/generate.py,
 bench/attention_bench.py and train/train.py import ``kernels`` from here. Skipped when the
@@ -21,7 +21,7 @@ import pytest
 
 from conftest import REPO
 
-RUNNER = os.path.join(REPO, "tests", "ref_callers.py")
+RUNNER = os.path.join(REPO, "baseline", "ref_callers.py")
 REF = os.path.join(REPO, "baseline", "_ref")
 
 pytestmark = pytest.mark.skipif(
