@@ -27,7 +27,6 @@ import json
 import os
 import statistics
 import sys
-import traceback
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(HERE)
@@ -56,7 +55,9 @@ def timed(fn, warmup: int = 3, rep: int = 10) -> float:
     return statistics.median(a.elapsed_time(b) for a, b in evs)
 
 
-def run_cases() -> dict:
+def run_cases(alloc=None) -> dict:
+    """Time each config; a config that fails records its error instead of a time."""
+    import triton
     from kernels.BlockSparseDecodeAttention import block_sparse_decode_attention
     from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
     from kernels.SplitKVDecodeAttention import split_kv_decode_attention
@@ -67,55 +68,74 @@ def run_cases() -> dict:
     def randn(*shape):
         return torch.empty(*shape, dtype=torch.bfloat16, device="cuda").normal_(generator=g)
 
-    # C2
-    B, n, bs = 8, 1024, 16
-    q, k, v = (randn(B, H, 2 * n, D).requires_grad_(True) for _ in range(3))
-    do = randn(B, H, 2 * n, D)
-    fwd_flops = 4.0 * D * (n * n + n * bs) * B * H
-    ms_f = timed(lambda: BlockSparseFlashAttention.apply(q, k, v, bs))
+    def case(name, fn):
+        try:
+            out[name] = fn()
+        except Exception as e:
+            out[name] = {"error": f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"}
+        torch.cuda.empty_cache()
 
-    def fwd_bwd():
-        o = BlockSparseFlashAttention.apply(q, k, v, bs)
-        torch.autograd.grad(o, (q, k, v), do)
-    ms_fb = timed(fwd_bwd)
-    out["c2_b8_n1024_bs16"] = {
-        "fwd_ms": round(ms_f, 4), "fwd_tflops": round(fwd_flops / ms_f / 1e9, 2),
-        "fwd_bwd_ms": round(ms_fb, 4), "fwd_bwd_tflops": round(3.5 * fwd_flops / ms_fb / 1e9, 2)}
-    del q, k, v, do
-    # C3
-    for b3, kv in ((32, 65536 + 16), (8, 16384 + 16)):
+    B, n, bs = 8, 1024, 16
+    fwd_flops = 4.0 * D * (n * n + n * bs) * B * H
+
+    def c2():
+        q, k, v = (randn(B, H, 2 * n, D).requires_grad_(True) for _ in range(3))
+        do = randn(B, H, 2 * n, D)
+        ms_f = timed(lambda: BlockSparseFlashAttention.apply(q, k, v, bs))
+        res = {"fwd_ms": round(ms_f, 4), "fwd_tflops": round(fwd_flops / ms_f / 1e9, 2)}
+
+        def fwd_bwd():
+            o = BlockSparseFlashAttention.apply(q, k, v, bs)
+            if alloc is not None:
+                # the backward runs in autograd's device thread, which does not see the
+                # allocator set in this thread: set it there too (a hook on O runs first)
+                o.register_hook(lambda grad: (triton.set_allocator(alloc), grad)[1])
+            torch.autograd.grad(o, (q, k, v), do)
+        try:
+            ms_fb = timed(fwd_bwd)
+            res.update({"fwd_bwd_ms": round(ms_fb, 4),
+                        "fwd_bwd_tflops": round(3.5 * fwd_flops / ms_fb / 1e9, 2)})
+        except Exception as e:
+            res["bwd_error"] = f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"
+        return res
+    case("c2_b8_n1024_bs16", c2)
+
+    def c3(b3, kv):
         qd, kd, vd = randn(b3, H, 16, D), randn(b3, H, kv, D), randn(b3, H, kv, D)
         ms = timed(lambda: split_kv_decode_attention(qd, kd, vd, bs))
         by = b3 * H * (256 * kv + 4096)
-        out[f"c3_splitkv_b{b3}_kv{(kv - 16) // 1024}k"] = {"us": round(ms * 1e3, 2),
-                                                            "GBps": round(by / ms / 1e6, 1)}
-        del qd, kd, vd
-    # prefill (block-causal, every row a query)
-    qp, kp, vp = randn(1, H, 3088, D), randn(1, H, 3088, D), randn(1, H, 3088, D)
-    ms = timed(lambda: block_sparse_decode_attention(qp, kp, vp, bs))
-    out["prefill_b1_3088"] = {"us": round(ms * 1e3, 2)}
+        return {"us": round(ms * 1e3, 2), "GBps": round(by / ms / 1e6, 1)}
+    for b3, kv in ((32, 65536 + 16), (8, 16384 + 16)):
+        case(f"c3_splitkv_b{b3}_kv{(kv - 16) // 1024}k", lambda b3=b3, kv=kv: c3(b3, kv))
+
+    def prefill():
+        qp, kp, vp = randn(1, H, 3088, D), randn(1, H, 3088, D), randn(1, H, 3088, D)
+        return {"us": round(timed(lambda: block_sparse_decode_attention(qp, kp, vp, bs)) * 1e3, 2)}
+    case("prefill_b1_3088", prefill)
     return out
 
 
 def main() -> None:
     import triton
     res = {"triton": triton.__version__, "gpu": torch.cuda.get_device_name()}
+    # as the reference runs: no allocator installed
+    from kernels.SplitKVDecodeAttention import split_kv_decode_attention
+    q = torch.randn(1, H, 16, D, dtype=torch.bfloat16, device="cuda")
+    k = torch.randn(1, H, 1040, D, dtype=torch.bfloat16, device="cuda")
     try:
+        split_kv_decode_attention(q, k, k, 16)
+        torch.cuda.synchronize()
+        res["as_is"] = "ran"
         res.update(run_cases())
         res["allocator"] = "none (as the reference runs)"
-    except Exception as e:  # record why the unchanged setup failed
+    except Exception as e:
         res["as_is_error"] = f"{type(e).__name__}: {str(e).splitlines()[0][:300]}"
-        if "allocator" not in str(e).lower():
-            res["traceback_tail"] = traceback.format_exc().splitlines()[-3:]
-            print(json.dumps(res), flush=True)
-            return
-        triton.set_allocator(
-            lambda size, align, stream: torch.empty(size, dtype=torch.int8, device="cuda"))
-        try:
-            res.update(run_cases())
-            res["allocator"] = "torch-backed, installed by this harness"
-        except Exception as e2:
-            res["error"] = f"{type(e2).__name__}: {str(e2).splitlines()[0][:300]}"
+
+        def alloc(size, align, stream):
+            return torch.empty(size, dtype=torch.int8, device="cuda")
+        triton.set_allocator(alloc)
+        res.update(run_cases(alloc))
+        res["allocator"] = "torch-backed, installed by this harness"
     print(json.dumps(res), flush=True)
 
 

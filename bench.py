@@ -773,7 +773,7 @@ def reference_extras() -> dict:
         loop = {"bsfa_tokens_per_s": round(loop["bsfa"]["tokens_per_s"]),
                 "custom_tokens_per_s": round(loop["custom"]["tokens_per_s"]),
                 "speedup": round(loop["bsfa"]["tokens_per_s"] / loop["custom"]["tokens_per_s"], 3),
-                "loss_max_rel_diff": round(loop["loss_max_rel_diff"], 5),
+                "loss_max_rel_diff": float(f"{loop['loss_max_rel_diff']:.3e}"),
                 "config": loop["config"]}
     out["train_loop"] = loop
     return out
