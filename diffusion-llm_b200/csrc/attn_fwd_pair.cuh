@@ -15,12 +15,13 @@
 //   warps 4-7  the same for the clean tile
 //   warp 8     TMA producer: each item's two Q tiles, then the K/V tiles of its steps
 //   warp 9     TMEM owner and UMMA issuer (one thread)
-// TMEM columns: three S buffers [0,128), [128,256), [256,384) used in rotation by the item's
-// S tiles in issue order (noisy before clean within a step), O_noisy [384,448), O_clean
-// [448,512). P (16-bit pairs) is written over the first 64 columns of its S buffer. The
-// issuer runs two S tiles ahead of the P V products: S(t) is issued once P V(t-3) has been
-// (it occupied the same buffer), so a warpgroup that publishes P(t) normally finds its next
-// S tile already computed. Within a diagonal tile, 32-column chunks no row of a warp can see
+// TMEM columns, per query tile x (0 noisy, 1 clean): S_x [128x, 128x+128), P_x (16-bit
+// pairs) [256+64x, 256+64x+64), O_x [384+64x, 384+64x+64). P has its own columns, so a
+// warpgroup releases S_x as soon as it has loaded the tile into registers, and the issuer
+// computes the next S_x while the warpgroup still works on the exponentials: a warpgroup
+// finds its next S tile computed when it finishes one, and the two warpgroups wait on
+// nothing of each other's. Per step the issuer issues the step's S tiles, then the previous
+// step's P V products. Within a diagonal tile, 32-column chunks no row of a warp can see
 // skip their exponentials and write P = 0.
 #pragma once
 
@@ -40,9 +41,9 @@ struct PairSmem {
   static constexpr uint32_t kV = kK + kPairStages * kTile16;
   static constexpr uint32_t kOut = kV + kPairStages * kTile16;    // [noisy, clean] O staging
   static constexpr uint32_t kBar = kOut + 2 * kTile16;
-  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], s_full[2][3], p_full[3],
-  // o_done[2], o_free[2]
-  static constexpr uint32_t kNumBars = 4 + 3 * kPairStages + 13;
+  // q_full[2], q_empty[2], k_full[S], v_full[S], kv_empty[S], and per query tile s_full,
+  // s_free, p_full, o_done, o_free
+  static constexpr uint32_t kNumBars = 4 + 3 * kPairStages + 10;
   static constexpr uint32_t kTmemSlot = kBar + kNumBars * 8;
   static constexpr uint32_t kBytes = kTmemSlot + 16;
   static constexpr uint32_t kAlloc = kBytes + 1024;  // room to align the base to 1 KB
@@ -145,14 +146,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint64_t* k_full = bars + 4;
   uint64_t* v_full = bars + 4 + kPairStages;
   uint64_t* kv_empty = bars + 4 + 2 * kPairStages;
-  // s_full[x][b] completes when an S tile of query tile x has landed in buffer b: one
-  // barrier per warpgroup and buffer, so a warpgroup only ever waits for the next phase of
-  // its own barriers (a shared barrier per buffer could be two phases behind a warpgroup
-  // whose previous tile used another buffer, and a parity wait cannot tell those apart)
-  uint64_t* s_full = bars + 4 + 3 * kPairStages;    // [noisy, clean][S buffer]
-  uint64_t* p_full = s_full + 6;                    // [S buffer]
-  uint64_t* o_done = s_full + 9;                    // [noisy, clean]
-  uint64_t* o_free = s_full + 11;                   // [noisy, clean]
+  // per query tile x; each barrier has one waiting side, which waits for every phase in
+  // turn, so a parity wait never meets a barrier two phases ahead
+  uint64_t* s_full = bars + 4 + 3 * kPairStages;    // S_x computed
+  uint64_t* s_free = s_full + 2;                    // S_x loaded by warpgroup x
+  uint64_t* p_full = s_full + 4;                    // P_x written
+  uint64_t* o_done = s_full + 6;                    // O_x += P_x V landed
+  uint64_t* o_free = s_full + 8;                    // O_x read by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PairSmem::kTmemSlot);
 
   const int warp = static_cast<int>(warp_id());
@@ -163,6 +163,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 128);
+      mbar_init(&p_full[i], 128);
       mbar_init(&o_done[i], 1);
       mbar_init(&o_free[i], 128);
     }
@@ -170,11 +173,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-    }
-    for (int b = 0; b < 3; ++b) {
-      mbar_init(&s_full[b], 1);
-      mbar_init(&s_full[3 + b], 1);
-      mbar_init(&p_full[b], 128);
     }
     fence_mbar_init();
   }
@@ -230,30 +228,33 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       constexpr uint32_t idesc_pv = idesc_f16(128, 64, false, true, kBF16);
       const uint32_t sbase = smem_u32(smem);
       bool ok = true;
-      // P V products waiting to be issued, oldest first (at most two behind the last S)
+      // P V products of the previous step, noisy first
       struct Pv {
-        int t, x, it, J;
-        bool first, last_in_step;
+        int x, it, J;
+        bool first, last;
       };
-      Pv pa{}, pb{};  // pending, oldest first
-      int nq = 0;
+      Pv pa{}, pb{};
+      int np = 0;
+      uint32_t s_issued = 0;  // bit x: an S tile of query tile x has been issued
+      uint32_t sf_par = 0;    // bit x: parity of the next s_free[x] phase to wait for
+      uint32_t pv_par = 0;    // bit x: parity of the next p_full[x] phase to wait for
       auto issue_pv = [&](const Pv& e) {
         const int st = e.J % kPairStages;
-        const int b = e.t % 3;
         ok = ok && mbar_wait(&v_full[st], (e.J / kPairStages) & 1);
         if (ok && e.first && e.it > 0) ok = mbar_wait(&o_free[e.x], (e.it - 1) & 1);
-        ok = ok && mbar_wait(&p_full[b], (e.t / 3) & 1);
+        ok = ok && mbar_wait(&p_full[e.x], (pv_par >> e.x) & 1u);
         if (!ok) return;
+        pv_par ^= 1u << e.x;
         tc_fence_after();
         const uint64_t vdesc = sw128_desc(sbase + PairSmem::kV + st * kTile16, kTile16, 1024);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tmem + 384 + e.x * 64, tmem + b * 128 + kk * 8, vdesc + ((kk * 2048) >> 4),
-                  idesc_pv, (!e.first || kk > 0) ? 1u : 0u);
+          umma_ts(tmem + 384 + e.x * 64, tmem + 256 + e.x * 64 + kk * 8,
+                  vdesc + ((kk * 2048) >> 4), idesc_pv, (!e.first || kk > 0) ? 1u : 0u);
         umma_commit(&o_done[e.x]);
-        if (e.last_in_step) umma_commit(&kv_empty[st]);
+        if (e.last) umma_commit(&kv_empty[st]);
       };
-      int t = 0, J = 0;
+      int J = 0;
       for (int it = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++it)) {
         int bh, i;
         pair_item(w, p.num_bh, num_pairs, &bh, &i);
@@ -272,36 +273,41 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tc_fence_after();
           const uint64_t kdesc = sw128_desc(sbase + PairSmem::kK + st * kTile16, 16, 1024);
           const int last_x = ps.need[1] ? 1 : 0;
-          for (int x = 0; x < 2 && ok; ++x) {
-            if (!ps.need[x]) continue;
-            const int b = t % 3;
+          Pv c0{}, c1{};
+          int nc = 0;
+#pragma unroll
+          for (int x = 0; x < 2; ++x) {
+            if (!ps.need[x] || !ok) continue;
+            if ((s_issued >> x) & 1u) {  // warpgroup x has loaded its previous S tile
+              ok = mbar_wait(&s_free[x], (sf_par >> x) & 1u);
+              if (!ok) break;
+              sf_par ^= 1u << x;
+              tc_fence_after();
+            }
+            s_issued |= 1u << x;
             const uint64_t qdesc =
                 sw128_desc(sbase + PairSmem::kQ + (qb * 2 + x) * kTile16, 16, 1024);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              umma_ss(tmem + b * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
+              umma_ss(tmem + x * 128, qdesc + ((kk * 32) >> 4), kdesc + ((kk * 32) >> 4),
                       idesc_qk, kk > 0 ? 1u : 0u);
-            umma_commit(&s_full[x * 3 + b]);
+            umma_commit(&s_full[x]);
             if (j == steps - 1 && x == last_x) umma_commit(&q_empty[qb]);
-            const Pv cur{t, x, it, J, first[x], x == last_x};
+            const Pv e{x, it, J, first[x], x == last_x};
+            if (nc == 0) c0 = e;
+            else c1 = e;
+            ++nc;
             first[x] = false;
-            ++t;
-            if (nq == 2) {  // issue P V(t-3) behind S(t-1)
-              issue_pv(pa);
-              pa = pb;
-              pb = cur;
-            } else if (nq == 1) {
-              pb = cur;
-              nq = 2;
-            } else {
-              pa = cur;
-              nq = 1;
-            }
           }
+          if (np >= 1 && ok) issue_pv(pa);
+          if (np == 2 && ok) issue_pv(pb);
+          pa = c0;
+          pb = c1;
+          np = nc;
         }
       }
-      if (nq >= 1 && ok) issue_pv(pa);
-      if (nq == 2 && ok) issue_pv(pb);
+      if (np >= 1 && ok) issue_pv(pa);
+      if (np == 2 && ok) issue_pv(pb);
     }
     __syncwarp();
   } else {
@@ -309,12 +315,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int x = warp >> 2;
     const int row = threadIdx.x & 127;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_base + x * 128;
+    const uint32_t tP = tmem + lane_base + 256 + x * 64;
     const uint32_t tO = tmem + lane_base + 384 + x * 64;
     const int shift = x == 0 ? 1 : 0;
     bool ok = true;
-    int t = 0;   // S tiles of both warpgroups issued before the current one
-    int pv = 0;  // P V products of this warpgroup's tile so far
-    uint32_t s_phase = 0;  // bit b: parity of the next phase of s_full[x][b] to wait for
+    int pv = 0;           // P V products of this warpgroup's tile so far
+    uint32_t s_par = 0;   // parity of the next s_full[x] phase
     for (int it = 0, w = persistent_item(0); w < num_items; w = persistent_item(++it)) {
       int bh, i;
       pair_item(w, p.num_bh, num_pairs, &bh, &i);
@@ -326,18 +333,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       int own = 0;
       for (int j = 0; j < pl.na + pl.nb && ok; ++j) {
         const PairStep ps = pair_step(pl, j, p.n);
-        if (x == 1 && ps.need[0]) ++t;  // the noisy tile's S of this step comes first
-        if (!ps.need[x]) {
-          if (x == 0 && ps.need[1]) ++t;
-          continue;
-        }
-        const int b = t % 3;
+        if (!ps.need[x]) continue;
         const int rule = ps.rule[x];
-        ok = mbar_wait_warp(&s_full[x * 3 + b], (s_phase >> b) & 1u);
+        ok = mbar_wait_warp(&s_full[x], s_par);
         if (!ok) break;
-        s_phase ^= 1u << b;
+        s_par ^= 1u;
         tc_fence_after();
-        const uint32_t tS = tmem + lane_base + b * 128;
         // this row's visible key columns of the tile, and which 32-column chunks any row of
         // the warp can see
         int lo = 0, hi = kFwdBN;
@@ -364,6 +365,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int k = 0; k < 32; ++k) xs[c * 32 + k] = __uint_as_float(r[c][k]);
           }
         }
+        tc_fence_before();
+        mbar_arrive(&s_free[x]);  // S is in registers: the issuer may compute the next one
         // chunks no row of the warp can see are neither masked nor reduced: their
         // exponentials are skipped below and P is 0 there
         const bool masked = rule != 0;
@@ -406,16 +409,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
             for (int k = 0; k < 16; ++k) pk[k] = 0u;
           }
-          tmem_st16(tS + c * 16, pk);  // P over the first 64 (already read) S columns
+          if (c == 0 && own > 0) {
+            // P_x and O_x are free once the previous O += P V has landed (normally long
+            // since: it was issued when this warpgroup published its previous P)
+            ok = mbar_wait_warp(&o_done[x], (pv - 1) & 1);
+            tc_fence_after();
+          }
+          tmem_st16(tP + c * 16, pk);
         }
+        if (!ok) break;
         const float2 a01 = __fadd2_rn(__fadd2_rn(acc[0], acc[1]), __fadd2_rn(acc[2], acc[3]));
         l_run = l_run * alpha + (a01.x + a01.y);
-        tmem_st_wait();
-        if (own > 0) {
-          ok = mbar_wait_warp(&o_done[x], (pv - 1) & 1);  // the previous O += P V has landed
-          if (!ok) break;
-          tc_fence_after();
-        }
         // the rescale's TMEM load/store is warp-collective: vote, and let the rows that do
         // not need it multiply by alpha = 1
         if (__any_sync(0xffffffffu, rescale)) {
@@ -431,14 +435,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               r[c2][k] = __float_as_uint(__uint_as_float(r[c2][k]) * alpha);
             tmem_st32(tO + c2 * 32, r[c2]);
           }
-          tmem_st_wait();
         }
+        tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_full[b]);
+        mbar_arrive(&p_full[x]);
         ++pv;
         ++own;
-        ++t;
-        if (x == 0 && ps.need[1]) ++t;
       }
       // ---- epilogue: the tile's last O += P V has landed; O / l out through a swizzled
       // shared-memory tile and one TMA store, the LSE to global memory ----
