@@ -46,6 +46,8 @@ SIGNATURES = {
                              _i64, _pi64, _i32, _vp]),
     "bd3_qkv_rope_cache": (_i32, [_vp, _pi64, _i64, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _i64,
                                   _vp, _vp, _vp, _pi64, _i64, _i64, _i32, _vp]),
+    "bd3_f32_to_f16_scaled": (_i32, [_vp, _vp, _vp, _pi64, _i64, _i64, _i64, _i64, _i64, _vp,
+                                     _vp, _vp, _vp, _vp, _vp]),
     "bd3_subs_sample": (_i32, [_vp, _pi64, _i64, _i64, _i64, _vp, _i64, ctypes.c_double,
                                ctypes.c_double, ctypes.c_uint64, ctypes.c_uint64, _vp, _vp, _i32,
                                _vp]),

@@ -88,6 +88,46 @@ def attn_bwd_raw(q, k, v, o, lse, do, block_size: int):
     return dq, dk, dv
 
 
+def f32_to_f16_scaled_raw(q, k, v):
+    """fp32 q, k, v (B, H, rows, 64) as fp16 at tf32's significand (bd3_f32_to_f16_scaled):
+    returns (q * 2^-a, k * 2^a, v * 2^-c in fp16, exps) with exps = (a, c, 2^c) fp32 on the
+    device. q may have another row count than k and v."""
+    _check_cuda(q, k, v)
+    q, k, v = (x if x.stride(-1) == 1 and x.data_ptr() % 16 == 0
+               and all(st % 4 == 0 for st in x.stride()[:-1]) else x.contiguous()
+               for x in (q, k, v))
+    B, H, Sq, D = q.shape
+    Skv = k.shape[2]
+    if k.shape != v.shape or k.shape[:2] != q.shape[:2] or k.shape[3] != D:
+        raise AssertionError("q, k, v must be (B, H, rows, head_dim) with k, v alike")
+    q16 = torch.empty((B, H, Sq, D), dtype=torch.float16, device=q.device)
+    k16 = torch.empty((B, H, Skv, D), dtype=torch.float16, device=q.device)
+    v16 = torch.empty_like(k16)
+    exps = torch.empty(3, dtype=torch.float32, device=q.device)
+    ws = torch.empty(4, dtype=torch.int32, device=q.device)
+    strides = i64_array(_s3(q) + _s3(k) + _s3(v))
+    with torch.cuda.device(q.device):
+        check("bd3_f32_to_f16_scaled", LIB.bd3_f32_to_f16_scaled(
+            _ptr(q), _ptr(k), _ptr(v), strides, B, H, Sq, Skv, D, _ptr(q16), _ptr(k16),
+            _ptr(v16), _ptr(exps), _ptr(ws), _stream(q)))
+    return q16, k16, v16, exps
+
+
+@torch.library.custom_op("bd3::f32_to_f16_scaled", mutates_args=())
+def f32_to_f16_scaled_op(q: torch.Tensor, k: torch.Tensor,
+                         v: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                                   torch.Tensor]:
+    return f32_to_f16_scaled_raw(q, k, v)
+
+
+@f32_to_f16_scaled_op.register_fake
+def _(q, k, v):
+    return (q.new_empty(tuple(q.shape), dtype=torch.float16),
+            k.new_empty(tuple(k.shape), dtype=torch.float16),
+            v.new_empty(tuple(v.shape), dtype=torch.float16),
+            q.new_empty((3,), dtype=torch.float32))
+
+
 def decode_plan(B, H, q_len, kv_len, block_size, q_pos0=-1, kv_pos0=0):
     ns = ctypes.c_int64(0)
     wb = ctypes.c_size_t(0)

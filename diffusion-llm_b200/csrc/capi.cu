@@ -15,6 +15,7 @@
 #include "attn_fwd.cuh"
 #include "attn_fwd_pair.cuh"
 #include "decode.cuh"
+#include "f32_scale.cuh"
 #include "kv_rope.cuh"
 #include "sampler.cuh"
 
@@ -777,6 +778,53 @@ int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out
   bd3::decode_combine_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0,
                                static_cast<cudaStream_t>(stream)>>>(c);
   return check_launch("decode_combine_kernel launch");
+}
+
+int bd3_f32_to_f16_scaled(const float* q, const float* k, const float* v, const int64_t* strides,
+                          int64_t B, int64_t H, int64_t q_rows, int64_t kv_rows, int64_t D,
+                          void* q16, void* k16, void* v16, float* exps, uint32_t* workspace,
+                          void* stream) {
+  if (B < 1 || H < 1 || q_rows < 1 || kv_rows < 1)
+    return fail(BD3_ERR_INVALID, "sizes must be >= 1");
+  if (D != 64) return fail(BD3_ERR_UNSUPPORTED, "head_dim must be 64 (got %lld)", (long long)D);
+  if (q_rows > (1LL << 30) || kv_rows > (1LL << 30) || B * H > (1LL << 24))
+    return fail(BD3_ERR_UNSUPPORTED, "too large");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  const float* src[3] = {q, k, v};
+  void* dst[3] = {q16, k16, v16};
+  bd3::F32ScaleParams p{};
+  for (int t = 0; t < 3; ++t) {
+    const int64_t* s3 = strides + 3 * t;
+    if (src[t] == nullptr || reinterpret_cast<uintptr_t>(src[t]) % 16 || s3[0] % 4 ||
+        s3[1] % 4 || s3[2] % 4)
+      return fail(BD3_ERR_INVALID, "fp32 inputs: pointer and strides must be 16-byte aligned");
+    if (dst[t] == nullptr || reinterpret_cast<uintptr_t>(dst[t]) % 8)
+      return fail(BD3_ERR_INVALID, "fp16 outputs must be 8-byte aligned");
+    p.src[t] = src[t];
+    p.dst[t] = static_cast<uint16_t*>(dst[t]);
+    p.sb[t] = s3[0];
+    p.sh[t] = s3[1];
+    p.ss[t] = s3[2];
+    p.rows[t] = static_cast<int>(t == 0 ? q_rows : kv_rows);
+  }
+  if (exps == nullptr || workspace == nullptr || reinterpret_cast<uintptr_t>(workspace) % 4)
+    return fail(BD3_ERR_WORKSPACE, "exps (3 floats) and workspace (3 uint32) are required");
+  p.ws = workspace;
+  p.exps = exps;
+  p.H = static_cast<int>(H);
+  p.bh = static_cast<int>(B * H);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(workspace, 0, 3 * sizeof(uint32_t), st);
+  if (e != cudaSuccess) return cuda_fail(e, "zeroing the maxima");
+  int sms = 148;
+  if (const int rc = current_device_sms(&sms); rc != BD3_OK) return rc;
+  const int64_t n4 = B * H * (q_rows > kv_rows ? q_rows : kv_rows) * 16;
+  int64_t blocks = (n4 + 255) / 256;
+  if (blocks > 4LL * sms) blocks = 4LL * sms;
+  bd3::f32_absmax_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  if (const int rc = check_launch("f32_absmax_kernel launch"); rc != BD3_OK) return rc;
+  bd3::f32_to_f16_scaled_kernel<<<static_cast<unsigned>(blocks), 256, 0, st>>>(p);
+  return check_launch("f32_to_f16_scaled_kernel launch");
 }
 
 int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, int64_t S,

@@ -13,7 +13,8 @@ by powers of two, which is exact, into fp16's range and then rounded:
   matching powers of two (chain rule through the three scalings).
 
 The exponents are computed on the device, so nothing waits on the host: torch.compile and
-CUDA graph capture see plain tensor ops around the custom ops. Where the two differ:
+CUDA graph capture see one custom op (two kernels, bd3_f32_to_f16_scaled) for the operands.
+Where the two differ:
 
 * values far below a tensor's maximum become fp16 subnormals or zero (absolute error below
   2^-25 of fp16's unit at the scaled maximum), which tf32 keeps normal;
@@ -26,23 +27,24 @@ from __future__ import annotations
 import torch
 from torch import Tensor
 
-F16_MAX = 65504.0
+from bd3attn import ops
 
 
 def exponent(t: Tensor) -> Tensor:
-    """floor(log2(max |t|)) as a 0-d fp32 tensor on t's device (-100 for an all-zero t)."""
-    return torch.floor(torch.log2(t.detach().abs().amax().float().clamp_min(2.0 ** -100)))
+    """floor(log2(max |t|)) as a 0-d fp32 tensor on t's device, exactly (from the binary
+    exponent), and at least -100."""
+    m = t.detach().abs().amax().float()
+    return (torch.frexp(m).exponent.float() - 1.0).clamp_min(-100.0)
 
 
 def qkv_to_f16(q: Tensor, k: Tensor, v: Tensor):
-    """(q16, k16, v16, a, c): q * 2^-a, k * 2^a, v * 2^-c rounded to fp16, and the
-    exponents a, c as 0-d fp32 device tensors."""
-    a = torch.floor((exponent(q) - exponent(k)) * 0.5)
-    c = exponent(v) - 4.0
-    q16 = (q * torch.exp2(-a)).clamp_(-F16_MAX, F16_MAX).to(torch.float16)
-    k16 = (k * torch.exp2(a)).clamp_(-F16_MAX, F16_MAX).to(torch.float16)
-    v16 = (v * torch.exp2(-c)).to(torch.float16)
-    return q16, k16, v16, a, c
+    """(q16, k16, v16, a, c): q * 2^-a, k * 2^a, v * 2^-c rounded to fp16 (q and k
+    saturated), and the exponents a, c as 0-d fp32 device tensors; one library call."""
+    if torch.compiler.is_compiling():
+        q16, k16, v16, exps = torch.ops.bd3.f32_to_f16_scaled(q, k, v)
+    else:
+        q16, k16, v16, exps = ops.f32_to_f16_scaled_raw(q, k, v)
+    return q16, k16, v16, exps[0], exps[1]
 
 
 def grad_to_f16(do: Tensor):

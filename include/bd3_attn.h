@@ -181,6 +181,20 @@ BD3_API int bd3_lse_merge(const float* parts, const float* lses, void* o, float*
  * cache_row0 < 0 takes the first cache row from the device value positions[0] (positions
  * required), so a CUDA graph captured once writes each new block at its own rows; a row
  * range outside [0, cache_rows) then writes nothing and sets status bit 4. */
+/* fp32 q, k, v onto the fp16 kernels at tf32's precision (the reference's Triton dots round
+ * fp32 operands to tf32, kernels/BlockSparseFlashAttention.py:45-70; it has no separate entry).
+ * q is (B, H, q_rows, 64), k and v (B, H, kv_rows, 64), fp32 with the last dim contiguous and
+ * element strides strides[0..2] (q), [3..5] (k), [6..8] (v); q16, k16, v16 are contiguous fp16
+ * outputs of the same shapes. With e_x = floor(log2(max |x|)) (at least -100),
+ * a = floor((e_q - e_k) / 2) and c = e_v - 4, writes q * 2^-a and k * 2^a (saturated at
+ * +-65504; the scores q . k are unchanged) and v * 2^-c, rounded to nearest, and
+ * exps = {a, c, 2^c} (fp32, device). O computed from the fp16 operands is O / 2^c.
+ * workspace: 3 uint32 of device memory, zeroed by this call. Enqueued on `stream`. */
+BD3_API int bd3_f32_to_f16_scaled(const float* q, const float* k, const float* v,
+                                  const int64_t* strides, int64_t B, int64_t H, int64_t q_rows,
+                                  int64_t kv_rows, int64_t D, void* q16, void* k16, void* v16,
+                                  float* exps, uint32_t* workspace, void* stream);
+
 BD3_API int bd3_qkv_rope_cache(const void* qkv, const int64_t* qkv_strides, int64_t B, int64_t S,
                                int64_t H, int64_t D, const int64_t* positions, int64_t pos0,
                                const float* cos_table, const float* sin_table, int64_t max_pos,
