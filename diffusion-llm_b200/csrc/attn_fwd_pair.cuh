@@ -352,11 +352,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
           if (__any_sync(0xffffffffu, hi > lo && hi > 32 * c && lo < 32 * c + 32)) vis |= 1u << c;
-        // pass 1: the row max (a chunk's values die as soon as it is reduced)
-        const bool masked = rule != 0;
-        float mx;
+        float xs[128];
         {
-          float xs[128];
           uint32_t r[4][32];
 #pragma unroll
           for (int c = 0; c < 4; ++c) tmem_ld32_async(tS + c * 32, r[c]);
@@ -367,13 +364,17 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
             for (int k = 0; k < 32; ++k) xs[c * 32 + k] = __uint_as_float(r[c][k]);
           }
-          // chunks no row of the warp can see are neither masked nor reduced: their
-          // exponentials are skipped below and P is 0 there
-          mx = max3(chunk_max<0>(xs, vis, masked, lo, hi), chunk_max<1>(xs, vis, masked, lo, hi),
-                    fmaxf(chunk_max<2>(xs, vis, masked, lo, hi),
-                          chunk_max<3>(xs, vis, masked, lo, hi))) *
-               p.scale_log2;
         }
+        tc_fence_before();
+        mbar_arrive(&s_free[x]);  // S is in registers: the issuer may compute the next one
+        // chunks no row of the warp can see are neither masked nor reduced: their
+        // exponentials are skipped below and P is 0 there
+        const bool masked = rule != 0;
+        const float mx = max3(chunk_max<0>(xs, vis, masked, lo, hi),
+                              chunk_max<1>(xs, vis, masked, lo, hi),
+                              fmaxf(chunk_max<2>(xs, vis, masked, lo, hi),
+                                    chunk_max<3>(xs, vis, masked, lo, hi))) *
+                         p.scale_log2;
         float alpha = 1.f;
         bool rescale = false;
         const float m_new = fmaxf(m_run, mx);
@@ -387,30 +388,15 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const float2 nm2 = make_float2(-m_use, -m_use);
         float2 acc[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f),
                          make_float2(0.f, 0.f)};
-        // pass 2: S again, 32 columns at a time, the next chunk's load in flight while this
-        // one's exponentials run; few live registers leave the compiler room to interleave
-        // the chunk's sixteen independent column pairs
-        uint32_t rc[2][32];
-        tmem_ld32_async(tS, rc[0]);
-        tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t(&cur)[32] = rc[c & 1];
-          if (c < 3) tmem_ld32_async(tS + (c + 1) * 32, rc[(c + 1) & 1]);
-          reg_fence(cur);
           uint32_t pk[16];
           if (vis & (1u << c)) {
-            if (masked) {
-#pragma unroll
-              for (int k = 0; k < 32; ++k)
-                if (32 * c + k < lo || 32 * c + k >= hi) cur[k] = __float_as_uint(-INFINITY);
-            }
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
               const int gi = c * 16 + k;  // column pair of the row
-              const float2 tt = __ffma2_rn(
-                  make_float2(__uint_as_float(cur[2 * k]), __uint_as_float(cur[2 * k + 1])),
-                  sc2, nm2);
+              const float2 tt =
+                  __ffma2_rn(make_float2(xs[2 * gi], xs[2 * gi + 1]), sc2, nm2);
               float2 e;
               if ((gi * kPairPoly) / 64 != ((gi + 1) * kPairPoly) / 64)
                 e = exp2_fma2(tt);
@@ -422,11 +408,6 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           } else {
 #pragma unroll
             for (int k = 0; k < 16; ++k) pk[k] = 0u;
-          }
-          if (c < 3) tmem_ld_wait();  // the next chunk has landed
-          if (c == 2) {
-            tc_fence_before();
-            mbar_arrive(&s_free[x]);  // all of S is in registers or done with
           }
           if (c == 0 && own > 0) {
             // P_x and O_x are free once the previous O += P V has landed (normally long
