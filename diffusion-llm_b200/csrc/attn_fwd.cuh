@@ -1,8 +1,11 @@
-// Block-sparse attention forward on tcgen05 tensor cores (sm_100a).
+// Block-sparse attention forward on tcgen05 tensor cores (sm_100a), one query tile per item.
 //
-// Replaces block_sparse_attention_fwd_kern (kernels/BlockSparseFlashAttention.py:76-172) for
-// the training layout, and block_sparse_decode_kern (kernels/BlockSparseDecodeAttention.py:
-// 41-110) for prefill-sized decode calls (q_len > 64).
+// Replaces block_sparse_decode_kern (kernels/BlockSparseDecodeAttention.py:41-110) for
+// prefill-sized decode calls (q_len > 64): the library instantiates it in kDecode mode. The
+// training layout (block_sparse_attention_fwd_kern, kernels/BlockSparseFlashAttention.py:
+// 76-172) runs on attn_fwd_pair_kernel (attn_fwd_pair.cuh), which serves both query tiles
+// that share a K/V stream at once; the kTrain branches below are that path's earlier form and
+// are not instantiated. This header also holds the constants and TMA helpers both share.
 //
 // Persistent: one CTA per SM steps through (batch*head, 128-row query tile) work items,
 // heaviest tiles first, with TMEM, barriers and the K/V ring kept across items and the Q tile
