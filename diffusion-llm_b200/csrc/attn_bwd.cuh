@@ -269,6 +269,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == 20) {
     // ---------------- TMA producer: per item K, V; per step Q_i, dO_i, L2_i, Delta_i --------
     if (elect_one()) {
+      const uint64_t keep = l2_policy_evict_last();
       bool ok = true;
       int it = 0, i = 0;
       for (int k = 0, w = persistent_item(0); w < num_items && ok; w = persistent_item(++k)) {
@@ -287,8 +288,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             if (i >= kBwdStages) ok = mbar_wait(&qd_empty[st], ((i / kBwdStages) - 1) & 1);
             if (!ok) break;
             mbar_expect_tx(&qd_full[st], 2 * kTile16 + 1024);
-            tma_load_4d(&tm_q, &qd_full[st], smem + BwdSmem::kQ + st * kTile16, 0, s, t.hh, t.bb);
-            tma_load_4d(&tm_do, &qd_full[st], smem + BwdSmem::kDO + st * kTile16, 0, s, t.hh, t.bb);
+            // Q and dO tiles are read again by every key tile of this (batch, head) that
+            // sees them: keep them in L2 ahead of the fp32 dQ accumulator's lines
+            tma_load_4d_hint(&tm_q, &qd_full[st], smem + BwdSmem::kQ + st * kTile16, 0, s, t.hh,
+                             t.bb, keep);
+            tma_load_4d_hint(&tm_do, &qd_full[st], smem + BwdSmem::kDO + st * kTile16, 0, s,
+                             t.hh, t.bb, keep);
             uint8_t* vec = smem + BwdSmem::kVec + st * 1024;
             bulk_load(vec, p.lse2 + t.row0 + s, 512, &qd_full[st]);
             bulk_load(vec + 512, p.delta + t.row0 + s, 512, &qd_full[st]);
