@@ -41,7 +41,7 @@ UNIT = "TFLOP/s"
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each training
 # kernel on the C2 workload at B=8, from one `ncu --set full` capture of that kernel. The
 # work is B x H independent (batch, head) slices, so the traffic scales with B.
-NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 319_690_752, "attn_fwd": 81_416_704}
+NCU_TRAFFIC_BYTES_B8 = {"bwd_fused": 323_849_728, "attn_fwd": 80_132_352}
 
 
 def nnz(n: int, bs: int) -> int:
