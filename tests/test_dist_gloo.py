@@ -132,10 +132,13 @@ def _dropout_worker(rank, world, port, leave_rank, leave_after, mode, out_dir):
         record["error"] = {"kind": "collective", "message": str(e)[:200]}
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
         json.dump(record, f)
-    if rank == 0 and mode == "watch":
+    if rank == 0:
         # the store's server lives in rank 0: keep it up until the peers have read it
         import time
-        time.sleep(0.5)
+        time.sleep(1.0)
+    # leave at once, as a rank that drops out does: the process group is not torn down, and
+    # letting the interpreter destroy it under its running threads can abort the process
+    os._exit(0)
 
 
 @pytest.mark.parametrize("mode", ["watch", "collective"])
