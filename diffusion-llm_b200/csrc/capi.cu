@@ -646,6 +646,8 @@ int bd3_decode_attn_devlen(const void* q, const void* k, const void* v, void* o,
 // capture. All calls share the one array and it keeps the last call's contents: nothing in it
 // needs to start at zero (every partial the combine step reads is written earlier in the same
 // call), but calls that overlap on the GPU (two streams, two host threads) race on it.
+// When the planner's split count needs more than the array, fewer splits are used (each
+// covering more key tiles), down to one split, which needs no scratch.
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB per device
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
 
@@ -685,11 +687,12 @@ int bd3_decode_attn_noalloc(const void* q, const void* k, const void* v, void* o
   if ((rc = bd3_decode_plan(B, H, q_len, kv_len, block_size, q_pos0, kv_pos0, &n_splits,
                             &need)) != BD3_OK)
     return rc;
-  if (need > kNoAllocScratchBytes)
-    return fail(BD3_ERR_UNSUPPORTED,
-                "no-alloc decode needs %zu bytes of scratch for %lld splits, more than its "
-                "fixed %zu bytes; use bd3_decode_attn with a workspace for this size",
-                need, (long long)n_splits, kNoAllocScratchBytes);
+  if (need > kNoAllocScratchBytes) {
+    // fewer splits need less scratch (one split needs none): take as many as the array holds
+    const size_t per_split = static_cast<size_t>(B * H * q_len) * (64 + 1) * 4;
+    n_splits = static_cast<int64_t>(kNoAllocScratchBytes / per_split);
+    if (n_splits < 1) n_splits = 1;
+  }
   float* scratch = nullptr;
   if ((rc = noalloc_scratch(&scratch)) != BD3_OK) return rc;
   return bd3_decode_attn(q, k, v, o, lse_out, B, H, q_len, kv_len, D, strides, block_size,

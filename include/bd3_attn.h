@@ -124,7 +124,8 @@ BD3_API int bd3_decode_attn_devlen(const void* q, const void* k, const void* v, 
  * allocator owns all device memory, or a decode loop that must not take the synchronisation
  * an allocation can imply. No counterpart in the reference. The split partials live in a
  * fixed 32 MiB array inside the library (held on every GPU that loads it until exit) instead
- * of a workspace; sizes whose partials need more are rejected with BD3_ERR_UNSUPPORTED.
+ * of a workspace; where the planner's split count needs more, fewer splits are used (down to
+ * one, which needs none), so every size runs, a little slower than with a workspace.
  * The first call on a device looks the array's address up (set-up work; make it before any
  * stream capture). Calls share the array, so calls that overlap on the GPU race.
  * q_len <= 64; the other arguments are those of bd3_decode_attn. */

@@ -88,21 +88,22 @@ def test_noalloc_matches_regular_twice(B, H, q_len, kv_len):
     assert_close("O after other inputs", o, ref_o, O_TOL)
 
 
-def test_noalloc_rejects_sizes_beyond_its_scratch():
-    """A request whose partials need more than the fixed array (here 64 queries x 16 splits x
-    384 heads, about 100 MB) is refused with a clear error. The buffers have the full claimed
-    shapes, so the call would stay in bounds even if it ran."""
+def test_noalloc_uses_fewer_splits_beyond_its_scratch():
+    """A shape whose planned partials need more than the fixed array (64 queries x 384 heads
+    over a 64K cache, about 100 MB at the planned split count) runs with fewer splits and
+    gives the regular entry point's result."""
     from bd3attn._lib import LIB
-    B, H, q_len, kv_len = 32, 12, 64, 65536
-    q = torch.empty(B, H, q_len, 64, device="cuda", dtype=torch.bfloat16)
-    k = torch.empty(B, H, kv_len, 64, device="cuda", dtype=torch.bfloat16)
-    v = torch.empty_like(k)
-    o = torch.empty_like(q)
-    rc = LIB.bd3_decode_attn_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                                     None, B, H, q_len, kv_len, 64, _strides(q, k, v, o), 16,
-                                     -1, 0, 0, 0, torch.cuda.current_stream().cuda_stream)
-    assert rc == 2  # BD3_ERR_UNSUPPORTED
-    msg = LIB.bd3_last_error().decode()
-    assert "scratch" in msg and "bd3_decode_attn" in msg
+    B, H, q_len, kv_len, bs = 32, 12, 64, 65536, 16
+    q, k, v = _inputs(5, B, H, q_len, kv_len)
+    need = ctypes.c_size_t(0)
+    n_splits = ctypes.c_int64(0)
+    assert LIB.bd3_decode_plan(B, H, q_len, kv_len, bs, -1, 0, ctypes.byref(n_splits),
+                               ctypes.byref(need)) == 0
+    assert need.value > 32 << 20  # the case this test is about
+    rc, o, lse = _noalloc(LIB, q, k, v, bs)
+    assert rc == 0, LIB.bd3_last_error().decode()
+    ref_o, ref_lse, _ = _regular(LIB, q, k, v, bs)
     torch.cuda.synchronize()
+    assert_close("O", o, ref_o, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
     assert_device_ok()
