@@ -105,8 +105,12 @@ def _dropout_worker(rank, world, port, leave_rank, leave_after, mode, out_dir):
     from bd3attn.dist import PeerWatch, RankDropped
     store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
                           timeout=datetime.timedelta(seconds=30))
+    # joining may take a while (each spawned rank imports the package first); only the
+    # data path's group carries the short timeout
     dist.init_process_group("gloo", store=store, rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=3))
+                            timeout=datetime.timedelta(seconds=60))
+    dist.barrier()
+    group = dist.new_group(list(range(world)), timeout=datetime.timedelta(seconds=3))
     watch = PeerWatch(store, rank, world, timeout_s=2.0)
     g = torch.Generator().manual_seed(0)
     q = torch.randn(1, 2, 16, 64, generator=g)
@@ -118,7 +122,7 @@ def _dropout_worker(rank, world, port, leave_rank, leave_after, mode, out_dir):
         for step in range(4):
             if mode == "watch":
                 watch.enter(step)
-            o, _ = sharded_decode(q, k[:, :, a:b], v[:, :, a:b], 16, a, 320,
+            o, _ = sharded_decode(q, k[:, :, a:b], v[:, :, a:b], 16, a, 320, group=group,
                                   out_dtype=torch.float64, partial_fn=_oracle_partial,
                                   merge_fn=_oracle_merge)
             record["steps_done"].append(step)
