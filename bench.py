@@ -279,11 +279,14 @@ def flush_l2(l2) -> None:
 
 
 def time_steps(fn, steps: int, l2) -> list[float]:
-    """Per-step device times (ms) of fn(), each after an L2 flush outside its events."""
+    """Per-step device times (ms) of fn(), each after an L2 flush outside its events. A short
+    device-side sleep after the flush keeps the GPU busy while the host issues fn()'s launches,
+    so a kernel of a few microseconds is timed on the device, not behind the Python call."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
     for s, e in evs:
         flush_l2(l2)
+        torch.cuda._sleep(100_000)  # ~50 us at 1.9 GHz, outside the events
         s.record()
         fn()
         e.record()
@@ -307,19 +310,7 @@ def decode_extras(ops, dev, l2, peaks, reps: int = 10) -> dict:
                                 "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
     del k3, v3
     # C4: live-block decode, B=16, kv 8192, 32 of 128 64-token blocks live per (b, h)
-    b4, kv4, nb, live = 16, 8192, 128, 32
-    q4 = torch.randn(b4, H, 16, D, generator=g).bfloat16().to(dev)
-    k4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
-    v4 = torch.randn(b4, H, kv4, D, generator=g).bfloat16().to(dev)
-    idx = torch.stack([torch.cat([torch.randperm(nb - 1, generator=g)[:live - 1].sort().values,
-                                  torch.tensor([nb - 1])]) for _ in range(b4 * H)])
-    idx = idx.view(b4, H, live).int().to(dev)
-    cnt = torch.full((b4, H), live, dtype=torch.int32, device=dev)
-    ms = time_steps(lambda: ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS), reps, l2)
-    by = b4 * H * (live * 64 * 256 + 4096)
-    t = statistics.median(ms)
-    out["live_b16_kv8k_25pct"] = {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
-                                  "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
+    out.update(live_decode_extras(dev, l2, peaks, reps))
     return out
 
 
@@ -440,8 +431,8 @@ def sharded_decode_extras(dev, l2, peaks, world: int, rank: int, reps: int = 10)
 
 
 def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
-    """Benchmark config 4 alone (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per
-    (b, h)), as decode_extras times it: the command the live-block ncu capture runs."""
+    """Benchmark config 4 (B=16, H=12, kv 8192, 32 of 128 64-token blocks live per (b, h)):
+    one call timed alone after an L2 flush, and per call inside a captured decode loop."""
     from bd3attn import ops
     g = torch.Generator().manual_seed(5)
     b4, kv4, nb, live = 16, 8192, 128, 32
@@ -452,13 +443,43 @@ def live_decode_extras(dev, l2, peaks, reps: int = 10) -> dict:
                                   torch.tensor([nb - 1])]) for _ in range(b4 * H)])
     idx = idx.view(b4, H, live).int().to(dev)
     cnt = torch.full((b4, H), live, dtype=torch.int32, device=dev)
-    for _ in range(3):
-        ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS)
-    ms = time_steps(lambda: ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS), reps, l2)
     by = b4 * H * (live * 64 * 256 + 4096)
-    t = statistics.median(ms)
-    return {"live_b16_kv8k_25pct": {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
-                                    "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}}
+    # three more caches of the same shape: the calls of a decode loop below read 4 x 403 MB
+    # of distinct memory in turn, so no call finds the previous one's blocks in L2
+    caches = [(k4, v4)] + [(torch.empty_like(k4).normal_(), torch.empty_like(v4).normal_())
+                           for _ in range(3)]
+    out = {}
+    # the planned launch (one CTA per (b, h) list at this size), then each list split in two
+    for name, ns in (("live_b16_kv8k_25pct", None), ("live_b16_kv8k_25pct_2_splits", 2)):
+        def run():
+            ops.live_decode_raw(q4, k4, v4, idx, cnt, 64, BS, n_splits=ns)
+        for _ in range(3):
+            run()
+        t = statistics.median(time_steps(run, reps, l2))
+        row = {"us": round(t * 1e3, 2), "GBps": round(by / t / 1e6, 1),
+               "frac_hbm": round(by / t / 1e6 / peaks["hbm_gbs"], 4)}
+        # per call in a decode loop: 16 calls over the four caches captured in one CUDA
+        # graph, so each launch overlaps the kernel before it (programmatic dependent launch)
+        # instead of adding its latency, as in a serving step
+        n_calls = 16
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(4):  # warm the allocator and the launch set-up outside the capture
+                ops.live_decode_raw(q4, caches[i][0], caches[i][1], idx, cnt, 64, BS, n_splits=ns)
+        torch.cuda.current_stream().wait_stream(side)
+        with torch.cuda.graph(graph):
+            for i in range(n_calls):
+                kc, vc = caches[i % 4]
+                ops.live_decode_raw(q4, kc, vc, idx, cnt, 64, BS, n_splits=ns)
+        graph.replay()
+        tg = statistics.median(time_steps(graph.replay, max(3, reps // 2), l2)) / n_calls
+        row.update({"us_in_graph_loop": round(tg * 1e3, 2),
+                    "frac_hbm_in_graph_loop": round(by / tg / 1e6 / peaks["hbm_gbs"], 4)})
+        del graph
+        out[name] = row
+    return out
 
 
 def kv_cache_extras(dev, l2, peaks, reps: int = 10) -> dict:

@@ -189,11 +189,13 @@ def _decode_devlen(q, k, v, block_size, kv_len_dev, out_dtype, return_lse):
 
 
 def live_decode_raw(q, k, v, live_idx, live_cnt, kv_block: int, block_size: int,
-                    out_dtype=None, return_lse: bool = False):
+                    out_dtype=None, return_lse: bool = False, n_splits: int | None = None):
     """Decode over a per-(batch, head) list of live KV blocks.
 
     live_idx: (B, H, max_live) int32 ascending block indices (entries past live_cnt ignored);
     live_cnt: (B, H) int32.
+    n_splits: None takes the planned split count; k >= 1 splits every (batch, head)'s list
+    over k CTAs (k > 1 merges their partials with the combine kernel).
     """
     _check_cuda(q, k, v, live_idx, live_cnt)
     q, k, v = _rows_contig(q), _rows_contig(k), _rows_contig(v)
@@ -207,6 +209,11 @@ def live_decode_raw(q, k, v, live_idx, live_cnt, kv_block: int, block_size: int,
     wb = ctypes.c_size_t(0)
     check("bd3_decode_live_plan", LIB.bd3_decode_live_plan(
         B, H, q_len, max_live, int(kv_block), ctypes.byref(ns), ctypes.byref(wb)))
+    if n_splits is not None:
+        if n_splits < 1:
+            raise ValueError("n_splits must be >= 1")
+        ns.value = int(n_splits)
+        wb.value = B * H * n_splits * q_len * 65 * 4 if n_splits > 1 else 0
     o = torch.empty((B, H, q_len, D), dtype=out_dtype, device=q.device)
     lse = torch.empty((B, H, q_len), dtype=torch.float32, device=q.device) if return_lse else None
     ws = torch.empty(max(wb.value, 16), dtype=torch.uint8, device=q.device)

@@ -109,6 +109,99 @@ __device__ __forceinline__ int dec_split_entries(const DecParams& p, int bh, int
   return left < 0 ? 0 : (left < p.tiles_per_split ? left : p.tiles_per_split);
 }
 
+// One 64-key K/V tile for the calling consumer warp (`warp` 0-3 takes keys [16 warp,
+// 16 warp + 16)): Q K^T and P V with mma.sync m16n8k16 and the online softmax of its rows
+// in registers. sk / sv: the tile's swizzled K and V in shared memory; the warp arrives on
+// `empty_bar` once its fragments are in registers. Keys at or past full_all are masked per
+// row against row_hi (the block-causal rule).
+template <int kMB, bool kBF16>
+__device__ __forceinline__ void dec_tile_step(uint32_t sk, uint32_t sv, uint64_t* empty_bar,
+                                              int warp, int lane, int key, int full_all,
+                                              const int (&row_hi)[kMB][2],
+                                              const uint32_t (&qa)[kMB][4][4],
+                                              float (&acc)[kMB][8][4], float (&m_run)[kMB][2],
+                                              float (&l_run)[kMB][2], float scale_log2) {
+  const int tq = lane & 3;
+  // K fragments for this warp's 16 keys: 2 n-tiles x 4 k-steps
+  uint32_t kb[4][4];
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    const int mi = lane >> 3;
+    const int krow = warp * 16 + (mi >> 1) * 8 + (lane & 7);
+    const int chunk = ks * 2 + (mi & 1);
+    ldsm_x4(sk + sw128_offset(krow, chunk), kb[ks][0], kb[ks][1], kb[ks][2], kb[ks][3]);
+  }
+  // V fragments (transposed): 8 D-tiles for one 16-key k-step
+  uint32_t vb[8][2];
+#pragma unroll
+  for (int dp = 0; dp < 4; ++dp) {
+    const int mi = lane >> 3;
+    const int vrow = warp * 16 + (mi & 1) * 8 + (lane & 7);
+    const int chunk = dp * 2 + (mi >> 1);
+    ldsm_x4_t(sv + sw128_offset(vrow, chunk), vb[2 * dp][0], vb[2 * dp][1],
+              vb[2 * dp + 1][0], vb[2 * dp + 1][1]);
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(empty_bar);
+
+  const int key0 = key + warp * 16;  // first key of this warp's slice
+  const bool partial = key0 + 16 > full_all;
+#pragma unroll
+  for (int mb = 0; mb < kMB; ++mb) {
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s[nt][i] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      mma16816<kBF16>(s[0], qa[mb][ks], kb[ks][0], kb[ks][1]);
+      mma16816<kBF16>(s[1], qa[mb][ks], kb[ks][2], kb[ks][3]);
+    }
+    if (partial) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = key0 + nt * 8 + 2 * tq + (i & 1);
+          if (c >= row_hi[mb][i >> 1]) s[nt][i] = -INFINITY;
+        }
+    }
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float mx = fmaxf(fmaxf(s[0][2 * hr], s[0][2 * hr + 1]), fmaxf(s[1][2 * hr], s[1][2 * hr + 1]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run[mb][hr], mx * scale_log2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2(m_run[mb][hr] - m_use);
+      m_run[mb][hr] = m_new;
+      float rs = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float e = ex2(fmaf(s[nt][2 * hr + i], scale_log2, -m_use));
+          s[nt][2 * hr + i] = e;
+          rs += e;
+        }
+      l_run[mb][hr] = l_run[mb][hr] * alpha + rs;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        acc[mb][nt][2 * hr] *= alpha;
+        acc[mb][nt][2 * hr + 1] *= alpha;
+      }
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<kBF16>(s[0][0], s[0][1]);
+    pa[1] = pack2<kBF16>(s[0][2], s[0][3]);
+    pa[2] = pack2<kBF16>(s[1][0], s[1][1]);
+    pa[3] = pack2<kBF16>(s[1][2], s[1][3]);
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) mma16816<kBF16>(acc[mb][nt], pa, vb[nt][0], vb[nt][1]);
+  }
+}
+
 struct DecSmem {
   static constexpr uint32_t kQ = 0;                            // up to 32 rows x 128 B
   static constexpr uint32_t kStage = 8192;                     // K then V, per stage
@@ -250,85 +343,8 @@ __global__ void __launch_bounds__(kDecThreads)
     ok = mbar_wait_warp(&full[st], (t / kDecStages) & 1);
     if (!ok) break;
     const uint32_t sk = sbase + DecSmem::kStage + st * 2 * kDecTile;
-    const uint32_t sv = sk + kDecTile;
-    // K fragments for this warp's 16 keys: 2 n-tiles x 4 k-steps
-    uint32_t kb[4][4];
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks) {
-      const int mi = lane >> 3;
-      const int krow = warp * 16 + (mi >> 1) * 8 + (lane & 7);
-      const int chunk = ks * 2 + (mi & 1);
-      ldsm_x4(sk + sw128_offset(krow, chunk), kb[ks][0], kb[ks][1], kb[ks][2], kb[ks][3]);
-    }
-    // V fragments (transposed): 8 D-tiles for one 16-key k-step
-    uint32_t vb[8][2];
-#pragma unroll
-    for (int dp = 0; dp < 4; ++dp) {
-      const int mi = lane >> 3;
-      const int vrow = warp * 16 + (mi & 1) * 8 + (lane & 7);
-      const int chunk = dp * 2 + (mi >> 1);
-      ldsm_x4_t(sv + sw128_offset(vrow, chunk), vb[2 * dp][0], vb[2 * dp][1],
-                vb[2 * dp + 1][0], vb[2 * dp + 1][1]);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-
-    const int key0 = key + warp * 16;  // first key of this warp's slice
-    const bool partial = key0 + 16 > full_all;
-#pragma unroll
-    for (int mb = 0; mb < kMB; ++mb) {
-      float s[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) s[nt][i] = 0.f;
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        mma16816<kBF16>(s[0], qa[mb][ks], kb[ks][0], kb[ks][1]);
-        mma16816<kBF16>(s[1], qa[mb][ks], kb[ks][2], kb[ks][3]);
-      }
-      if (partial) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int c = key0 + nt * 8 + 2 * tq + (i & 1);
-            if (c >= row_hi[mb][i >> 1]) s[nt][i] = -INFINITY;
-          }
-      }
-#pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        float mx = fmaxf(fmaxf(s[0][2 * hr], s[0][2 * hr + 1]), fmaxf(s[1][2 * hr], s[1][2 * hr + 1]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float m_new = fmaxf(m_run[mb][hr], mx * p.scale_log2);
-        const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-        const float alpha = ex2(m_run[mb][hr] - m_use);
-        m_run[mb][hr] = m_new;
-        float rs = 0.f;
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int i = 0; i < 2; ++i) {
-            const float e = ex2(fmaf(s[nt][2 * hr + i], p.scale_log2, -m_use));
-            s[nt][2 * hr + i] = e;
-            rs += e;
-          }
-        l_run[mb][hr] = l_run[mb][hr] * alpha + rs;
-#pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          acc[mb][nt][2 * hr] *= alpha;
-          acc[mb][nt][2 * hr + 1] *= alpha;
-        }
-      }
-      uint32_t pa[4];
-      pa[0] = pack2<kBF16>(s[0][0], s[0][1]);
-      pa[1] = pack2<kBF16>(s[0][2], s[0][3]);
-      pa[2] = pack2<kBF16>(s[1][0], s[1][1]);
-      pa[3] = pack2<kBF16>(s[1][2], s[1][3]);
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) mma16816<kBF16>(acc[mb][nt], pa, vb[nt][0], vb[nt][1]);
-    }
+    dec_tile_step<kMB, kBF16>(sk, sk + kDecTile, &empty[st], warp, lane, key, full_all, row_hi,
+                              qa, acc, m_run, l_run, p.scale_log2);
   }
 
   // ---------------- merge the four warps' states ----------------

@@ -105,6 +105,59 @@ def test_live_blocks_matches_oracle(B, H, kv_len, n_blocks_live, kv_block):
     assert_close("O", o[:sub_b], ref, O_TOL)
 
 
+def _ragged_lists(B, H, nb, max_live, seed, empty_every=0):
+    """Ascending live block lists with ragged counts (some empty when empty_every > 0); the
+    query block nb - 1 is live in every non-empty list."""
+    rng = np.random.default_rng(seed)
+    live = np.zeros((B, H, max_live), dtype=np.int32)
+    cnt = np.zeros((B, H), dtype=np.int32)
+    for b in range(B):
+        for h in range(H):
+            if empty_every and (b * H + h) % empty_every == 1:
+                continue
+            c = int(rng.integers(1, max_live + 1))
+            pick = rng.choice(nb - 1, size=c - 1, replace=False) if c > 1 else []
+            live[b, h, :c] = sorted(list(pick) + [nb - 1])
+            cnt[b, h] = c
+    return live, cnt
+
+
+@pytest.mark.parametrize("B,H,q_len,kv_len,max_live,kv_block,empty_every", [
+    (16, 12, 16, 8192, 32, 64, 0),     # benchmark config 4 shape, ragged counts
+    (16, 12, 16, 8192, 32, 64, 5),     # some (batch, head) lists empty
+    (2, 3, 32, 1000, 4, 128, 0),       # two 16-row groups, 128-token blocks
+    (1, 2, 7, 4096, 64, 64, 0),        # few (batch, head) pairs: the plan splits the lists
+])
+def test_live_split_counts_agree(B, H, q_len, kv_len, max_live, kv_block, empty_every):
+    """Live-block decode with one CTA per (batch, head) list, with the list split over 2 and 3
+    CTAs (partials merged by the combine kernel) and with the planned split count agree with
+    each other and with the oracle within the stated tolerances; an empty list gives NaN and
+    LSE -inf. Splits round P to bf16 against different running maxima, so they agree to about
+    1e-3, not bit for bit."""
+    from bd3attn import ops
+    q, k, v = qkv(11, B, H, q_len, kv_len)
+    nb = -(-kv_len // kv_block)
+    live, cnt = _ragged_lists(B, H, nb, max_live, 3, empty_every)
+    args = (q.cuda(), k.cuda(), v.cuda(), torch.from_numpy(live).cuda(),
+            torch.from_numpy(cnt).cuda(), kv_block, 16)
+    has = torch.from_numpy(cnt > 0)
+    o1, l1 = ops.live_decode_raw(*args, out_dtype=torch.float32, return_lse=True, n_splits=1)
+    assert_device_ok()
+    for ns in (None, 2, 3):
+        o, lse = ops.live_decode_raw(*args, out_dtype=torch.float32, return_lse=True, n_splits=ns)
+        assert_device_ok()
+        assert torch.isnan(o.cpu()[~has]).all() and (lse.cpu()[~has] == float("-inf")).all()
+        assert_close(f"O {ns} splits vs 1", o.cpu()[has], o1.cpu()[has], 2e-3)
+        assert_close(f"LSE {ns} splits vs 1", lse.cpu()[has], l1.cpu()[has], 1e-4)
+    sub = [(b, h) for b in range(min(B, 2)) for h in range(H) if cnt[b, h] > 0]
+    lists = [[live[b, h, :cnt[b, h]].tolist() for h in range(H)] for b in range(min(B, 2))]
+    mask = oracle.live_block_mask(lists, q_len, kv_len, kv_block, 16)
+    ref, ref_lse = oracle.attention(q[:2], k[:2], v[:2], mask)
+    for b, h in sub:
+        assert_close("O vs oracle", o1[b, h], ref[b, h], O_TOL)
+        assert_close("LSE vs oracle", l1[b, h], ref_lse[b, h], LSE_TOL)
+
+
 def test_lse_merge_of_shards_equals_full():
     """Sequence-sharded decode: per-shard partial (O fp32, LSE) then the merge kernel."""
     from bd3attn import ops
