@@ -844,11 +844,30 @@ def run_ours(args) -> None:
     achieved = algo / (dom_ms * 1e-3) / 1e12
     launches = sum(c for _, c in prof.values())
 
+    # the deterministic backward (torch.use_deterministic_algorithms(True)): dQ's partials
+    # added as 64-bit fixed-point integers; same protocol, reported beside
+    def step_det():
+        o, lse = ops.attn_fwd_raw(q, k, v, BS)
+        ops.attn_bwd_raw(q, k, v, o, lse, do, BS, deterministic=True)
+    for _ in range(3):
+        step_det()
+    barrier(world)
+    ms_det = time_steps(step_det, args.steps, l2)
+    ops.profile_enable(True)
+    time_steps(step_det, args.steps, l2)
+    prof_det = ops.profile_collect()
+    ops.profile_enable(False)
+    barrier(world)
+    det_row = {"tflops": round((fwd_f + bwd_f) / (statistics.mean(ms_det) * 1e-3) / 1e12, 2),
+               "ms_per_step": round(statistics.mean(ms_det), 4),
+               "kernels_ms_per_launch": {kk: round(t / c, 4) for kk, (t, c) in prof_det.items()}}
+
     if args.kernels_only:
         if rank == 0:
             print(json.dumps({"metric": METRIC, "value": round(value, 3), "unit": UNIT,
                               "kernels_ms_per_launch": {kk: round(t / c, 4)
-                                                        for kk, (t, c) in prof.items()}}))
+                                                        for kk, (t, c) in prof.items()},
+                              "deterministic_dq": det_row}))
         return
 
     # bs = 4 (the other block size of config 2), same protocol, reported beside
@@ -979,6 +998,7 @@ def run_ours(args) -> None:
     extra = {"fwd_ms": round(prof["attn_fwd"][0] / prof["attn_fwd"][1], 4),
              "kernels_ms_per_launch": {kk: round(t / c, 4) for kk, (t, c) in prof.items()},
              "bs4_tflops": round(bs4, 2),
+             "deterministic_dq": det_row,
              "dense_equiv_fwd_tflops_ref_convention": round(
                  4.0 * B * H * (2 * N_HALF) ** 2 * D / (prof["attn_fwd"][0] / prof["attn_fwd"][1]
                                                          * 1e-3) / 1e12, 2)}

@@ -29,7 +29,10 @@ SIGNATURES = {
     "bd3_attn_fwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _pi64, _i64, _i32,
                             _vp]),
     "bd3_attn_bwd_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "bd3_attn_bwd_det_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
     "bd3_attn_bwd": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                            _pi64, _i64, _i32, _vp, _sz, _vp]),
+    "bd3_attn_bwd_det": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                             _pi64, _i64, _i32, _vp, _sz, _vp]),
     "bd3_decode_plan": (_i32, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _psz]),
     "bd3_decode_attn": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64,

@@ -67,21 +67,26 @@ def attn_fwd_raw(q, k, v, block_size: int):
     return o, lse
 
 
-def attn_bwd_raw(q, k, v, o, lse, do, block_size: int):
-    """(dQ, dK, dV) of BD3-LM training attention."""
+def attn_bwd_raw(q, k, v, o, lse, do, block_size: int, deterministic: bool = False):
+    """(dQ, dK, dV) of BD3-LM training attention. deterministic: dQ's partials are added as
+    64-bit fixed-point integers (bd3_attn_bwd_det), so dQ is the same on every run; otherwise
+    they are added in fp32 in the order the key tiles finish."""
     _check_cuda(q, k, v, o, lse, do)
     q, k, v, o, do = (_rows_contig(t) for t in (q, k, v, o, do))
     B, H, S, D = q.shape
     dq = torch.empty((B, H, S, D), dtype=q.dtype, device=q.device)
     dk = torch.empty_like(dq)
     dv = torch.empty_like(dq)
-    ws_bytes = LIB.bd3_attn_bwd_workspace_size(B, H, S // 2, D)
+    size_fn, fn, name = ((LIB.bd3_attn_bwd_det_workspace_size, LIB.bd3_attn_bwd_det,
+                          "bd3_attn_bwd_det") if deterministic else
+                         (LIB.bd3_attn_bwd_workspace_size, LIB.bd3_attn_bwd, "bd3_attn_bwd"))
+    ws_bytes = size_fn(B, H, S // 2, D)
     ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=q.device)
     lse = lse.contiguous()
     strides = i64_array(_s3(q) + _s3(k) + _s3(v) + _s3(o) + _s3(do) + _s3(dq) + _s3(dk)
                         + _s3(dv))
     with torch.cuda.device(q.device):
-        check("bd3_attn_bwd", LIB.bd3_attn_bwd(
+        check(name, fn(
             _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse), _ptr(do), _ptr(dq), _ptr(dk),
             _ptr(dv), B, H, S // 2, D, strides, int(block_size), _code(q.dtype), _ptr(ws),
             ws.numel(), _stream(q)))
@@ -288,13 +293,13 @@ def _(q, k, v, block_size):
 
 @torch.library.custom_op("bd3::attn_bwd", mutates_args=())
 def attn_bwd_op(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor,
-                lse: torch.Tensor, do: torch.Tensor,
-                block_size: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    return attn_bwd_raw(q, k, v, o, lse, do, block_size)
+                lse: torch.Tensor, do: torch.Tensor, block_size: int,
+                deterministic: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    return attn_bwd_raw(q, k, v, o, lse, do, block_size, deterministic)
 
 
 @attn_bwd_op.register_fake
-def _(q, k, v, o, lse, do, block_size):
+def _(q, k, v, o, lse, do, block_size, deterministic):
     shape = tuple(q.shape)
     return q.new_empty(shape), q.new_empty(shape), q.new_empty(shape)
 

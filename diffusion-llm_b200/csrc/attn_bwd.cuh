@@ -19,6 +19,14 @@
 //                       warpgroup through TMA reduce-adds (cp.reduce.async.bulk.tensor).
 //   bwd_dq_convert_kernel  dQ = scale * accumulator, in the input dtype.
 //
+// Deterministic variant (kDet, bd3_attn_bwd_det): the fp32 reduce-adds make dQ's last bits
+// depend on the order in which key tiles finish. With kDet each dQ_i partial is rounded to a
+// 64-bit integer in units of 2^-32 and added with integer bulk reductions
+// (cp.reduce.async.bulk .add.u64), which are associative, so dQ is the same on every run, as
+// the reference's dQ kernel (:369-452), which loops over key tiles in order, is. A partial of
+// magnitude 2^20 or more (or NaN) sets device status bit 8 instead of wrapping silently;
+// 2^20 * 2^32 summed over up to 2^10 key tiles stays inside the 63-bit range.
+//
 // Each 128-query step runs as two 64-query halves whose S^T/dP^T live in two TMEM buffers, so
 // the MMAs of one half overlap the element-wise pass over the other. K/V are double-buffered
 // across items (the next item's tiles load during the current one), the step and half-step
@@ -58,6 +66,9 @@ struct BwdParams {
   float* delta;          // (B, H, 2n), written by bwd_prep_kernel
   float* lse2;           // (B, H, 2n), LSE * log2(e), written by bwd_prep_kernel
   float* dq_acc;         // (B, H, 2n, 64) fp32, zeroed by bwd_prep_kernel
+  // kDet: per 128-query tile T, four 16 KB blocks (columns [16b, 16b+16)) of 128 rows x 16
+  // int64 (2^-32 units), each row's 16-byte chunks swizzled as sw128_offset; zeroed likewise
+  unsigned long long* dq_fix;
   void* dq;
   void* dk;
   void* dv;
@@ -97,6 +108,16 @@ __device__ __forceinline__ void bulk_wait_group0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// 1-D bulk reduce-add of `bytes` of int64 (two's complement, added as u64) from shared
+// memory into global memory, tracked by the issuing thread's bulk async-group.
+__device__ __forceinline__ void bulk_reduce_add_u64(unsigned long long* dst, const void* src,
+                                                    uint32_t bytes) {
+  asm volatile("cp.reduce.async.bulk.global.shared::cta.bulk_group.add.u64 [%0], [%1], %2;" ::"l"(
+                   dst),
+               "r"(smem_u32(src)), "r"(bytes)
+               : "memory");
+}
+
 // 1-D bulk copy global -> shared completing on an mbarrier (16-byte aligned, size % 16 == 0).
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
                                           uint64_t* bar) {
@@ -108,7 +129,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 
 // Delta, LSE*log2(e) and the dQ accumulator's zeroing; 8 threads per query row.
-template <bool kBF16>
+template <bool kBF16, bool kDet>
 __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdParams p, int rows_total) {
   const int gid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gid >> 3, part = gid & 7;
@@ -128,9 +149,15 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdParams p, int ro
       acc = fmaf(x.x, y.x, acc);
       acc = fmaf(x.y, y.y, acc);
     }
-    float4* z = reinterpret_cast<float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
-    z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-    z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (kDet) {  // 64 bytes of the int64 accumulator per thread (any layout)
+      float4* z = reinterpret_cast<float4*>(p.dq_fix + static_cast<long long>(gid) * 8);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) z[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      float4* z = reinterpret_cast<float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
+      z[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+      z[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
@@ -142,7 +169,7 @@ __global__ void __launch_bounds__(256) bwd_prep_kernel(const BwdParams p, int ro
 }
 
 // dQ = scale * accumulator in the output dtype; 8 threads per query row.
-template <bool kBF16>
+template <bool kBF16, bool kDet>
 __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const BwdParams p, int rows_total) {
   const int gid = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = gid >> 3, part = gid & 7;
@@ -150,8 +177,29 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const BwdParams p, 
   const int S = 2 * p.n;
   const int bh = row / S, r = row % S;
   const int bb = bh / p.H, hh = bh % p.H;
-  const float4* src = reinterpret_cast<const float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
-  const float4 x = src[0], y = src[1];
+  float4 x, y;
+  if constexpr (kDet) {
+    // columns [8 part, 8 part + 8): block part / 2, 16-byte chunks 4 (part % 2) .. + 3 of the
+    // row, each at its swizzled position
+    const int rt = row & 127;
+    const unsigned long long* blk =
+        p.dq_fix + static_cast<long long>(row >> 7) * 8192 + (part >> 1) * 2048 + rt * 16;
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int c = 4 * (part & 1) + k;
+      const longlong2 w = *reinterpret_cast<const longlong2*>(blk + 2 * (c ^ (rt & 7)));
+      v[2 * k] = __ll2float_rn(w.x) * 2.3283064365386963e-10f;  // 2^-32
+      v[2 * k + 1] = __ll2float_rn(w.y) * 2.3283064365386963e-10f;
+    }
+    x = make_float4(v[0], v[1], v[2], v[3]);
+    y = make_float4(v[4], v[5], v[6], v[7]);
+  } else {
+    const float4* src =
+        reinterpret_cast<const float4*>(p.dq_acc + static_cast<long long>(row) * 64 + part * 8);
+    x = src[0];
+    y = src[1];
+  }
   const float s = p.scale;
   *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.dq) + bb * p.dq_sb + hh * p.dq_sh +
                             r * p.dq_ss + part * 8) =
@@ -208,7 +256,7 @@ __device__ __forceinline__ void bwd_item(int w, const BwdParams& p, BwdItem* t) 
   t->nsteps = ns;
 }
 
-template <bool kBF16>
+template <bool kBF16, bool kDet>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     bwd_fused_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                      const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -495,15 +543,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
           }
           ok = agree(mbar_wait_warp(dq_full, i & 1));
+          const uint32_t tdq = tmem + lane_base + tDQ;
           if (!ok) break;
           tc_fence_after();
+          if constexpr (kDet) {
+            // dQ_i in 64-bit fixed point: four 16-column rounds through the box, each one
+            // bulk integer reduce-add of its 16 KB block (the box's bytes as they are)
+            unsigned long long* blk = p.dq_fix + ((t.row0 + s) >> 7) * 8192;
+#pragma unroll 1
+            for (int b = 0; b < 4; ++b) {
+              if (leader) bulk_wait_group_read0();  // the previous bulk op has read the box
+              asm volatile("bar.sync 2, 128;" ::: "memory");
+              uint32_t r[16];
+              tmem_ld16_async(tdq + 16 * b, r);
+              tmem_ld_wait();
+              reg_fence(r);
+              if (b == 3) {
+                tc_fence_before();
+                mbar_arrive(dq_empty);
+              }
+              bool bad = false;
+              long long qv[16];
+#pragma unroll
+              for (int k = 0; k < 16; ++k) {
+                const float v = __uint_as_float(r[k]);
+                bad |= !(fabsf(v) < 1048576.f);  // 2^20; NaN too
+                qv[k] = __float2ll_rn(v * 4294967296.f);
+              }
+              if (bad) atomicOr(&g_bd3_status, kStatusFixedRange);
+#pragma unroll
+              for (int c = 0; c < 8; ++c)
+                *reinterpret_cast<longlong2*>(stage + sw128_offset(row, c)) =
+                    make_longlong2(qv[2 * c], qv[2 * c + 1]);
+              fence_proxy_async_smem();
+              asm volatile("bar.sync 2, 128;" ::: "memory");
+              if (leader) {
+                bulk_reduce_add_u64(blk + b * 2048, stage, kTile16);
+                bulk_commit_group();
+              }
+            }
+            continue;
+          }
           // the two 32-column halves of dQ_i go through the box in turn
 #pragma unroll
           for (int b = 0; b < 2; ++b) {
             if (leader) bulk_wait_group_read0();  // the previous bulk op has read the box
             asm volatile("bar.sync 2, 128;" ::: "memory");
             uint32_t r[32];
-            tmem_ld32_async(tmem + lane_base + tDQ + 32 * b, r);
+            tmem_ld32_async(tdq + 32 * b, r);
             tmem_ld_wait();
             reg_fence(r);
             if (b == 1) {

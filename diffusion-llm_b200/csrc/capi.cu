@@ -343,10 +343,20 @@ size_t bd3_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D) {
   return static_cast<size_t>(B * H * 2 * n) * (1 + 1 + 64) * sizeof(float);
 }
 
-int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
-                 const void* dout, void* dq, void* dk, void* dv, int64_t B, int64_t H,
-                 int64_t n, int64_t D, const int64_t* strides, int64_t block_size, int dtype,
-                 void* workspace, size_t workspace_bytes, void* stream) {
+size_t bd3_attn_bwd_det_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D) {
+  (void)D;
+  if (B < 1 || H < 1 || n < 1) return 0;
+  // Delta and LSE*log2(e) per query row, then the int64 fixed-point dQ accumulator
+  return static_cast<size_t>(B * H * 2 * n) * (2 * sizeof(float) + 64 * sizeof(int64_t));
+}
+
+}  // extern "C"
+
+namespace {
+int launch_bwd(bool det, const void* q, const void* k, const void* v, const void* o,
+               const float* lse, const void* dout, void* dq, void* dk, void* dv, int64_t B,
+               int64_t H, int64_t n, int64_t D, const int64_t* strides, int64_t block_size,
+               int dtype, void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_dims(B, H, D, dtype);
   if (rc != BD3_OK) return rc;
   if (n < 1 || n % bd3::kBwdBKV != 0)
@@ -355,7 +365,8 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   if (block_size < 1 || n % block_size != 0)
     return fail(BD3_ERR_INVALID, "n must be a multiple of block_size (n=%lld, block_size=%lld)",
                 (long long)n, (long long)block_size);
-  const size_t need = bd3_attn_bwd_workspace_size(B, H, n, D);
+  const size_t need = det ? bd3_attn_bwd_det_workspace_size(B, H, n, D)
+                          : bd3_attn_bwd_workspace_size(B, H, n, D);
   if (workspace == nullptr || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 16)
     return fail(BD3_ERR_WORKSPACE, "backward workspace too small: need %zu bytes, got %zu", need,
                 workspace_bytes);
@@ -401,6 +412,7 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   p.delta = static_cast<float*>(workspace);
   p.lse2 = p.delta + rows;
   p.dq_acc = p.lse2 + rows;
+  p.dq_fix = reinterpret_cast<unsigned long long*>(p.lse2 + rows);  // kDet: the int64 accumulator
   p.dq = dq;
   p.dk = dk;
   p.dv = dv;
@@ -421,8 +433,9 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   const unsigned eblocks = static_cast<unsigned>((rows * 8 + 255) / 256);
   {
     ProfScope ps(kPfDelta, st);
-    if (bf) bd3::bwd_prep_kernel<true><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
-    else bd3::bwd_prep_kernel<false><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    auto prep = bf ? (det ? bd3::bwd_prep_kernel<true, true> : bd3::bwd_prep_kernel<true, false>)
+                   : (det ? bd3::bwd_prep_kernel<false, true> : bd3::bwd_prep_kernel<false, false>);
+    prep<<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
   }
   if ((rc = check_launch("bwd_prep_kernel launch")) != BD3_OK) return rc;
   const int64_t items = B * H * p.num_tiles;
@@ -430,8 +443,10 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   int sms = 148;
   if ((rc = current_device_sms(&sms)) != BD3_OK) return rc;
   const unsigned grid = static_cast<unsigned>(items < sms ? items : sms);  // persistent
-  auto fused = bf ? bd3::bwd_fused_kernel<true> : bd3::bwd_fused_kernel<false>;
-  if ((rc = set_smem(fused, bd3::BwdSmem::kAlloc, 6 + (bf ? 0 : 1))) != BD3_OK) return rc;
+  auto fused = bf ? (det ? bd3::bwd_fused_kernel<true, true> : bd3::bwd_fused_kernel<true, false>)
+                  : (det ? bd3::bwd_fused_kernel<false, true> : bd3::bwd_fused_kernel<false, false>);
+  if ((rc = set_smem(fused, bd3::BwdSmem::kAlloc, (det ? 18 : 6) + (bf ? 0 : 1))) != BD3_OK)
+    return rc;
   {
     ProfScope ps(kPfDkdv, st);
     fused<<<grid, bd3::kBwdThreads, bd3::BwdSmem::kAlloc, st>>>(tq, tk, tv, tdo, tdqa, tdk, tdv, p);
@@ -439,10 +454,33 @@ int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, con
   if ((rc = check_launch("bwd_fused_kernel launch")) != BD3_OK) return rc;
   {
     ProfScope ps(kPfDq, st);
-    if (bf) bd3::bwd_dq_convert_kernel<true><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
-    else bd3::bwd_dq_convert_kernel<false><<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
+    auto conv = bf ? (det ? bd3::bwd_dq_convert_kernel<true, true>
+                          : bd3::bwd_dq_convert_kernel<true, false>)
+                   : (det ? bd3::bwd_dq_convert_kernel<false, true>
+                          : bd3::bwd_dq_convert_kernel<false, false>);
+    conv<<<eblocks, 256, 0, st>>>(p, static_cast<int>(rows));
   }
   return check_launch("bwd_dq_convert_kernel launch");
+}
+}  // namespace
+
+extern "C" {
+
+int bd3_attn_bwd(const void* q, const void* k, const void* v, const void* o, const float* lse,
+                 const void* dout, void* dq, void* dk, void* dv, int64_t B, int64_t H,
+                 int64_t n, int64_t D, const int64_t* strides, int64_t block_size, int dtype,
+                 void* workspace, size_t workspace_bytes, void* stream) {
+  return launch_bwd(false, q, k, v, o, lse, dout, dq, dk, dv, B, H, n, D, strides, block_size,
+                    dtype, workspace, workspace_bytes, stream);
+}
+
+int bd3_attn_bwd_det(const void* q, const void* k, const void* v, const void* o,
+                     const float* lse, const void* dout, void* dq, void* dk, void* dv, int64_t B,
+                     int64_t H, int64_t n, int64_t D, const int64_t* strides,
+                     int64_t block_size, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream) {
+  return launch_bwd(true, q, k, v, o, lse, dout, dq, dk, dv, B, H, n, D, strides, block_size,
+                    dtype, workspace, workspace_bytes, stream);
 }
 
 int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t block_size,

@@ -25,6 +25,7 @@ namespace bd3 {
 enum : unsigned {
   kStatusWaitTimeout = 1u,   // an mbarrier wait ran out of time
   kStatusBadLaunch = 2u,     // a kernel saw launch parameters it cannot handle
+  kStatusFixedRange = 8u,    // a dQ partial outside the deterministic backward's fixed-point range
 };
 __device__ unsigned int g_bd3_status;
 // Where the first bounded wait that ran out gave up: [0] set flag, [1] block, [2] thread,

@@ -81,10 +81,13 @@ class BlockSparseFlashAttention(torch.autograd.Function):
             dO, e = _precision.grad_to_f16(dO)
         else:
             dO = dO.to(q.dtype)
+        # torch.use_deterministic_algorithms(True) selects the backward whose dQ is the same
+        # on every run (fixed-point accumulation), as the reference's dQ kernel's is
+        det = torch.are_deterministic_algorithms_enabled()
         if torch.compiler.is_compiling():
-            dq, dk, dv = torch.ops.bd3.attn_bwd(q, k, v, O, L, dO, int(block_size))
+            dq, dk, dv = torch.ops.bd3.attn_bwd(q, k, v, O, L, dO, int(block_size), det)
         else:
-            dq, dk, dv = ops.attn_bwd_raw(q, k, v, O, L, dO, int(block_size))
+            dq, dk, dv = ops.attn_bwd_raw(q, k, v, O, L, dO, int(block_size), det)
         if ctx.scaled:
             # the kernel got 2^-e dO = 2^-(c+e) * (2^c dO), and 2^c dO is the cotangent of
             # O' = 2^-c O, so its gradients are 2^-(c+e) times those of q', k', v'

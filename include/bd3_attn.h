@@ -44,7 +44,8 @@ BD3_API int bd3_version(void);
 BD3_API const char* bd3_last_error(void);
 /* Sticky device-side status bits of the current device (1: a bounded wait inside a kernel
  * ran out; 2: a kernel rejected its launch parameters; 4: a RoPE position was outside the
- * table). Synchronises the device. Clears the
+ * table; 8: a dQ partial left the deterministic backward's fixed-point range). Synchronises
+ * the device. Clears the
  * bits when `clear` is non-zero. Returns a negative value if the CUDA call itself failed. */
 BD3_API int bd3_device_status(int clear);
 
@@ -77,6 +78,21 @@ BD3_API int bd3_attn_bwd(const void* q, const void* k, const void* v, const void
                  const void* dout, void* dq, void* dk, void* dv, int64_t B, int64_t H,
                  int64_t n, int64_t D, const int64_t* strides, int64_t block_size, int dtype,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Deterministic training attention backward: bd3_attn_bwd with dQ the same on every run, as
+ * the reference's dQ kernel (kernels/BlockSparseFlashAttention.py:369-452, a loop over key
+ * tiles in order) gives it. Each key tile's dQ partial is rounded to an int64 in units of
+ * 2^-32 and the partials are added as integers, so their order does not matter. A partial of
+ * magnitude 2^20 or more (or NaN) sets device status bit 8 (its sum would leave the 63-bit
+ * range). Arguments as bd3_attn_bwd; workspace: bd3_attn_bwd_det_workspace_size() bytes
+ * (520 per query row). The Python binding takes this path when
+ * torch.are_deterministic_algorithms_enabled(). */
+BD3_API size_t bd3_attn_bwd_det_workspace_size(int64_t B, int64_t H, int64_t n, int64_t D);
+BD3_API int bd3_attn_bwd_det(const void* q, const void* k, const void* v, const void* o,
+                             const float* lse, const void* dout, void* dq, void* dk, void* dv,
+                             int64_t B, int64_t H, int64_t n, int64_t D, const int64_t* strides,
+                             int64_t block_size, int dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Decode attention: the q_len queries attend kv_len keys under the block-causal rule

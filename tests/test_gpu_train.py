@@ -57,11 +57,37 @@ def test_backward_matches_oracle(B, H, n, bs):
 
 def test_dkdv_deterministic():
     """dK and dV are bitwise reproducible (one CTA owns each key tile and writes it once);
-    dQ is an fp32 atomic sum, equal up to summation order."""
+    by default dQ is an fp32 atomic sum, equal up to summation order."""
     _, (_, dq1, dk1, dv1) = _run(2, 2, 256, 16, seed=5)
     _, (_, dq2, dk2, dv2) = _run(2, 2, 256, 16, seed=5)
     assert torch.equal(dk1, dk2) and torch.equal(dv1, dv2)
     assert (dq1.float() - dq2.float()).abs().max().item() <= 1e-2
+
+
+@pytest.mark.parametrize("B,H,n,bs", [(2, 2, 256, 16), (1, 1, 128, 1), (1, 2, 1024, 4),
+                                      (16, 12, 256, 16), (8, 12, 1024, 16)])
+def test_deterministic_backward(B, H, n, bs):
+    """Under torch.use_deterministic_algorithms(True) the backward adds dQ's partials as
+    64-bit fixed-point integers: dQ, dK and dV are bitwise equal from run to run (the
+    reference's dQ kernel is deterministic too), and equal the fp32-accumulating backward's
+    within bf16 rounding and the oracle's within the stated tolerance."""
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True)
+    try:
+        (q, k, v, do), (o, dq1, dk1, dv1) = _run(B, H, n, bs, seed=5)
+        for _ in range(2):
+            _, (_, dq2, dk2, dv2) = _run(B, H, n, bs, seed=5)
+            assert torch.equal(dq1, dq2) and torch.equal(dk1, dk2) and torch.equal(dv1, dv2)
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    _, (_, dqf, dkf, dvf) = _run(B, H, n, bs, seed=5)
+    assert torch.equal(dk1, dkf) and torch.equal(dv1, dvf)  # the same kernel for dK, dV
+    # the two round the same sums (in different orders, or not) to bf16: one ulp apart at most
+    rel = ((dq1.float() - dqf.float()).abs() / dqf.float().abs().clamp_min(1.0)).max().item()
+    assert rel <= 1e-2, f"dQ det vs fp32 accumulation: relative {rel:.3e}"
+    if B * H * n <= 4096:
+        rdq, _, _ = oracle.attention_grads(q, k, v, do, oracle.block_diff_mask(n, bs))
+        assert_close("dQ det vs oracle", dq1, rdq, GRAD_TOL)
 
 
 @pytest.mark.parametrize("bs", [4, 16, 128])
