@@ -802,6 +802,13 @@ def reference_extras() -> dict:
 
 def run_ours(args) -> None:
     world, rank, local = dist_setup(args.gpus)
+    # the whole process (and the threads it starts: autograd's device thread, the clock
+    # sampler) on the GPU's NUMA-local cores: the e2e loop is paced by the host's launches
+    # between copies, and on a shared machine a thread that wanders onto a busy core made
+    # its steps up to 5x slower
+    local_cpus = gpu_local_cpus(local)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
     from bd3attn import ops
     from kernels.BlockSparseFlashAttention import BlockSparseFlashAttention
 
@@ -888,16 +895,9 @@ def run_ours(args) -> None:
     # the last copy out; each step's working set (~250 MB) is larger than L2.
     # The pinned buffers are allocated (first touched) from the GPU's NUMA-local cores, so
     # the copies do not cross the socket interconnect.
-    saved_cpus = os.sched_getaffinity(0)
-    local_cpus = gpu_local_cpus(local)
-    if local_cpus:
-        os.sched_setaffinity(0, local_cpus)
-    try:
-        host = [t.cpu().pin_memory() for t in (q, k, v, do)]
-        outs = [[torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
-                for _ in range(2)]
-    finally:
-        os.sched_setaffinity(0, saved_cpus)
+    host = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    outs = [[torch.empty(q.shape, dtype=q.dtype).pin_memory() for _ in range(3)]
+            for _ in range(2)]
     dbuf = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
 
     def link_gbps(dst, src, reps: int = 3) -> float:
