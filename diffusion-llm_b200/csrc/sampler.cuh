@@ -180,6 +180,28 @@ __device__ __forceinline__ void stage_row(const uint16_t* g16, int V, int n_chun
   }
 }
 
+// exp of a non-positive bf16 value, rounded to bf16, by table: rnd(expf(a)) for every a with
+// |a| in [2^-9, 128), indexed by a's magnitude bits minus 0x3B00 (2^-9) plus one, with entry 0
+// = 1.0 (every |a| below 2^-9: expf rounds to 1.0 there) and entry kExpTab - 1 = 0.0 (|a| of
+// 128 or more, -inf included: expf underflows bf16 from |a| = 93 on). Built per CTA with the
+// same expf the per-entry path calls, so the values are those of that path, bit for bit.
+constexpr int kExpTab = 2048 + 2;
+__device__ __forceinline__ void build_exp_tab(uint16_t* tab) {
+  for (int i = threadIdx.x; i < kExpTab; i += blockDim.x) {
+    float e;
+    if (i == 0) e = 1.f;
+    else if (i == kExpTab - 1) e = 0.f;
+    else e = expf(__uint_as_float((0x8000u | (0x3B00u + static_cast<uint32_t>(i - 1))) << 16));
+    tab[i] = static_cast<uint16_t>(__float_as_uint(rnd<0>(e)) >> 16);
+  }
+}
+// rnd(expf(a)) for the bf16 a in the low 16 bits of `bits` (a <= 0)
+__device__ __forceinline__ float exp_tab_lookup(const uint16_t* tab, uint32_t bits) {
+  int i = static_cast<int>(bits & 0x7FFFu) - 0x3B00 + 1;
+  i = i < 0 ? 0 : (i > kExpTab - 1 ? kExpTab - 1 : i);
+  return __uint_as_float(static_cast<uint32_t>(tab[i]) << 16);
+}
+
 // (score, index) with the larger score, the smaller index on a tie (torch.argmax's first max).
 __device__ __forceinline__ void best_of(double& s, int& i, double s2, int i2) {
   if (s2 > s || (s2 == s && i2 < i)) s = s2, i = i2;
@@ -208,6 +230,7 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   __shared__ int ri[kSampleThreads / 32];
   __shared__ double walk_q[kWalkChunks * kChunk];  // the claimed slice's weights
   __shared__ int walk_owner;
+  __shared__ uint16_t exp_tab[kStage ? kExpTab : 1];
   const int row = blockIdx.x;
   const int b = row / p.S, i = row % p.S;
   const long long tok = p.xt[static_cast<long long>(b) * p.S + i];
@@ -230,6 +253,7 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   uint4* const schunk = reinterpret_cast<uint4*>(srow_raw);
   if constexpr (kStage) {
     static_assert(kDtype == 0, "staging holds bf16 rows");
+    build_exp_tab(exp_tab);
     stage_row(reinterpret_cast<const uint16_t*>(lrow), p.V, n_chunks, schunk);
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -277,19 +301,35 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
     }
   }
   mx = block_max(mx, red);
-  // pass 2: sum of exp(x - max), each op rounded to the dtype
+  // pass 2: sum of exp(x - max), each op rounded to the dtype. Staged rows: the rounded
+  // x - max replaces x in shared memory (pass 3 and the walk start from it) and the
+  // exponential comes from the table
   float sum = 0.f;
   for (int c = threadIdx.x; c < n_chunks; c += kSampleThreads) {
-    float x[kChunk];
-    chunk(c, x);
+    if constexpr (kStage) {
+      const uint4 v = schunk[c];
+      uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < kChunk; k += 2) {
-      float a = x[k] - mx, bb = x[k + 1] - mx;
-      rnd2<kDtype>(a, bb);
-      a = expf(a), bb = expf(bb);
-      rnd2<kDtype>(a, bb);
-      sum += a;
-      sum += bb;
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat162 a2 = __floats2bfloat162_rn(__uint_as_float(w[k] << 16) - mx,
+                                                        __uint_as_float(w[k] & 0xffff0000u) - mx);
+        w[k] = *reinterpret_cast<const uint32_t*>(&a2);
+        sum += exp_tab_lookup(exp_tab, w[k]);
+        sum += exp_tab_lookup(exp_tab, w[k] >> 16);
+      }
+      schunk[c] = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+      float x[kChunk];
+      chunk(c, x);
+#pragma unroll
+      for (int k = 0; k < kChunk; k += 2) {
+        float a = x[k] - mx, bb = x[k + 1] - mx;
+        rnd2<kDtype>(a, bb);
+        a = expf(a), bb = expf(bb);
+        rnd2<kDtype>(a, bb);
+        sum += a;
+        sum += bb;
+      }
     }
   }
   sum = rnd<kDtype>(block_sum(sum, red));
@@ -304,18 +344,31 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   }
   // q of the 8 entries of chunk c (0 past the vocabulary)
   auto chunk_q = [&](int c, double (&q)[kChunk]) {
-    float x[kChunk];
-    chunk(c, x);
+    if constexpr (kStage) {  // the staged row holds rnd(x - max) after pass 2
+      const uint4 v = schunk[c];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int k = 0; k < kChunk; k += 2) {
-      float a = x[k] - mx, bb = x[k + 1] - mx;
-      rnd2<kDtype>(a, bb);
-      a -= lse, bb -= lse;
-      rnd2<kDtype>(a, bb);
-      a = expf(a), bb = expf(bb);
-      rnd2<kDtype>(a, bb);
-      q[k] = static_cast<double>(a) * keep;
-      q[k + 1] = static_cast<double>(bb) * keep;
+      for (int k = 0; k < 4; ++k) {
+        const __nv_bfloat162 l2 = __floats2bfloat162_rn(__uint_as_float(w[k] << 16) - lse,
+                                                        __uint_as_float(w[k] & 0xffff0000u) - lse);
+        const uint32_t lw = *reinterpret_cast<const uint32_t*>(&l2);
+        q[2 * k] = static_cast<double>(exp_tab_lookup(exp_tab, lw)) * keep;
+        q[2 * k + 1] = static_cast<double>(exp_tab_lookup(exp_tab, lw >> 16)) * keep;
+      }
+    } else {
+      float x[kChunk];
+      chunk(c, x);
+#pragma unroll
+      for (int k = 0; k < kChunk; k += 2) {
+        float a = x[k] - mx, bb = x[k + 1] - mx;
+        rnd2<kDtype>(a, bb);
+        a -= lse, bb -= lse;
+        rnd2<kDtype>(a, bb);
+        a = expf(a), bb = expf(bb);
+        rnd2<kDtype>(a, bb);
+        q[k] = static_cast<double>(a) * keep;
+        q[k + 1] = static_cast<double>(bb) * keep;
+      }
     }
     if (c == mask / kChunk) {
 #pragma unroll
@@ -325,11 +378,16 @@ __global__ void __launch_bounds__(kSampleThreads) subs_sample_kernel(const Sampl
   };
   auto q64 = [&](int j) -> double {
     if (j == mask) return stay;
-    float x;
-    if constexpr (kStage) x = __uint_as_float(static_cast<uint32_t>(srow_raw[j]) << 16);
-    else x = logit_at<kDtype>(lrow, j);
-    const float lp = rnd<kDtype>(rnd<kDtype>(x - mx) - lse);
-    return static_cast<double>(rnd<kDtype>(expf(lp))) * keep;
+    if constexpr (kStage) {  // the staged row holds rnd(x - max) after pass 2
+      const float a = __uint_as_float(static_cast<uint32_t>(srow_raw[j]) << 16);
+      const float lp = rnd<kDtype>(a - lse);
+      return static_cast<double>(
+                 exp_tab_lookup(exp_tab, __float_as_uint(lp) >> 16)) * keep;
+    } else {
+      const float x = logit_at<kDtype>(lrow, j);
+      const float lp = rnd<kDtype>(rnd<kDtype>(x - mx) - lse);
+      return static_cast<double>(rnd<kDtype>(expf(lp))) * keep;
+    }
   };
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
   long long pick;
