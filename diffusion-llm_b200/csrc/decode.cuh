@@ -202,6 +202,31 @@ __device__ __forceinline__ void dec_tile_step(uint32_t sk, uint32_t sv, uint64_t
   }
 }
 
+// ---- thread-block clusters (the split merge of a small decode) ----
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The address of this CTA's shared-memory word `addr` in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 struct DecSmem {
   static constexpr uint32_t kQ = 0;                            // up to 32 rows x 128 B
   static constexpr uint32_t kStage = 8192;                     // K then V, per stage
@@ -212,7 +237,12 @@ struct DecSmem {
   static constexpr uint32_t kAlloc = kBytes + 1024;
 };
 
-template <int kMB, bool kBF16, bool kLive>
+// kCluster: the n_splits CTAs of a (batch*head, row group) form one thread-block cluster
+// (2 <= n_splits <= 16). Each writes its partial (O normalised over its keys, natural-log LSE)
+// into its own shared memory; after a cluster barrier the cluster's CTA 0 merges the partials
+// through distributed shared memory in split order (the merge of decode_combine_kernel) and
+// writes O, so no combine launch and no workspace are needed.
+template <int kMB, bool kBF16, bool kLive, bool kCluster = false>
 __global__ void __launch_bounds__(kDecThreads)
     decode_kernel(const __grid_constant__ CUtensorMap tm_q,
                   const __grid_constant__ CUtensorMap tm_k,
@@ -299,6 +329,11 @@ __global__ void __launch_bounds__(kDecThreads)
         tma_load_4d(&tm_v, &full[st], sk + kDecTile, 0, key, hh, bb);
       }
     }
+    if constexpr (kCluster) {  // the cluster's barriers count every thread of every CTA
+      __syncwarp();
+      cluster_sync_all();
+      cluster_sync_all();
+    }
     return;  // the producer takes no part in the merge below
   }
 
@@ -379,8 +414,11 @@ __global__ void __launch_bounds__(kDecThreads)
       }
     }
   asm volatile("bar.sync 1, 128;" ::: "memory");
-  if (!ok) return;
+  if (!kCluster && !ok) return;
 
+  // kCluster: this split's partial, after the warps' states in the ring area
+  float* s_po = s_o + 4 * kRows * 64;   // [kRows][64] O normalised over this split's keys
+  float* s_pl = s_po + kRows * 64;      // [kRows] natural-log LSE (-inf: no key)
   const bool direct = (p.n_splits == 1);
   for (int idx = threadIdx.x; idx < kRows * 8; idx += 128) {
     const int rl = idx >> 3, c8 = (idx & 7) * 8;
@@ -405,6 +443,14 @@ __global__ void __launch_bounds__(kDecThreads)
     }
     const float inv = 1.f / L;
     const float lse = (M_use + __log2f(L)) * 0.69314718055994530942f;
+    if constexpr (kCluster) {
+      *reinterpret_cast<float4*>(&s_po[rl * 64 + c8]) =
+          make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+      *reinterpret_cast<float4*>(&s_po[rl * 64 + c8 + 4]) =
+          make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+      if (c8 == 0) s_pl[rl] = (L > 0.f) ? lse : -INFINITY;
+      continue;
+    }
     if (direct) {
       if (p.out_f32) {
         float* dst = reinterpret_cast<float*>(p.o) + bb * p.o_sb + hh * p.o_sh + r * p.o_ss + c8;
@@ -424,6 +470,51 @@ __global__ void __launch_bounds__(kDecThreads)
       *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
       if (c8 == 0) p.ws_lse[slot] = (L > 0.f) ? lse : -INFINITY;
     }
+  }
+  if constexpr (kCluster) {
+    __syncwarp();
+    cluster_sync_all();  // every split's partial is in its CTA's shared memory
+    if (split == 0 && ok) {
+      // merge the splits in order: weights exp(LSE_s - max LSE); an empty split (LSE = -inf)
+      // weighs 0 and is not read; a row with no key at all gets NaN, as the combine gives
+      const uint32_t po = smem_u32(s_po), pl = smem_u32(s_pl);
+      for (int idx = threadIdx.x; idx < kRows * 8; idx += 128) {
+        const int rl = idx >> 3, c8 = (idx & 7) * 8;
+        const int r = row0 + rl;
+        if (r >= p.q_len) continue;
+        float M = -INFINITY;
+        for (int sp = 0; sp < p.n_splits; ++sp)
+          M = fmaxf(M, dsmem_ld(dsmem_addr(pl + rl * 4, sp)));
+        const float M_use = (M == -INFINITY) ? 0.f : M;
+        float W = 0.f, o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
+        for (int sp = 0; sp < p.n_splits; ++sp) {
+          const float w = __expf(dsmem_ld(dsmem_addr(pl + rl * 4, sp)) - M_use);
+          if (w == 0.f) continue;
+          W += w;
+          const uint32_t a = dsmem_addr(po + (rl * 64 + c8) * 4, sp);
+          const float4 x = dsmem_ld4(a), y = dsmem_ld4(a + 16);
+          o[0] += w * x.x; o[1] += w * x.y; o[2] += w * x.z; o[3] += w * x.w;
+          o[4] += w * y.x; o[5] += w * y.y; o[6] += w * y.z; o[7] += w * y.w;
+        }
+        const float inv = 1.f / W;
+        if (p.out_f32) {
+          float* dst = reinterpret_cast<float*>(p.o) + bb * p.o_sb + hh * p.o_sh + r * p.o_ss + c8;
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+        } else {
+          uint16_t* dst = reinterpret_cast<uint16_t*>(p.o) + bb * p.o_sb + hh * p.o_sh + r * p.o_ss + c8;
+          *reinterpret_cast<uint4*>(dst) =
+              make_uint4(pack2<kBF16>(o[0] * inv, o[1] * inv), pack2<kBF16>(o[2] * inv, o[3] * inv),
+                         pack2<kBF16>(o[4] * inv, o[5] * inv), pack2<kBF16>(o[6] * inv, o[7] * inv));
+        }
+        if (p.lse != nullptr && c8 == 0)
+          p.lse[static_cast<long long>(bh) * p.q_len + r] = M_use + __logf(W);
+      }
+    }
+    __syncwarp();
+    cluster_sync_all();  // CTA 0 has read every partial: the others may exit
   }
 }
 

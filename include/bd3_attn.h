@@ -102,7 +102,11 @@ BD3_API int bd3_attn_bwd_det(const void* q, const void* k, const void* v, const 
  * Replaces split_kv_decode_attention (kernels/SplitKVDecodeAttention.py:130-171) and
  * block_sparse_decode_attention (kernels/BlockSparseDecodeAttention.py:118-148):
  * q_len <= 64 runs the split-KV kernel plus (when n_splits > 1) the LSE combine; longer
- * query blocks (prefill) run the tcgen05 block-causal kernel and need n_splits == 1.
+ * query blocks (prefill) run the tcgen05 block-causal kernel and need n_splits == 1. When 2 to
+ * 16 splits of a grid that fits on the GPU at once are asked for, the splits of each
+ * (batch*head, row group) run as one thread-block cluster and merge through distributed
+ * shared memory inside the kernel (no combine launch, no workspace: the plan then reports 0
+ * bytes).
  *   q: (B, H, q_len, 64); k, v: (B, H, kv_len, 64); o: (B, H, q_len, 64) in out_dtype.
  *   strides[12] = q, k, v, o (batch, head, seq) in elements.
  *   lse_out: optional (B*H, q_len) fp32 natural-log LSE of each row (NULL to skip).

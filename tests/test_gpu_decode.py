@@ -31,8 +31,10 @@ def test_split_kv_matches_oracle(B, H, q_len, kv_len, bs):
     assert_close("O", o, ref, O_TOL)
 
 
-@pytest.mark.parametrize("n_splits", [1, 2, 3, 7, 17])
+@pytest.mark.parametrize("n_splits", [1, 2, 3, 7, 8, 9, 16, 17, 24])
 def test_split_counts_and_lse(n_splits):
+    """2 to 16 splits are merged inside the kernel through a thread-block cluster, more by
+    the combine kernel: every count gives the oracle's O and LSE."""
     from bd3attn import ops
     q, k, v = qkv(4, 2, 3, 16, 1040)
     o, lse = ops.decode_raw(q.cuda(), k.cuda(), v.cuda(), 16, return_lse=True, n_splits=n_splits)
@@ -40,6 +42,26 @@ def test_split_counts_and_lse(n_splits):
     ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(16, 1040, 16))
     assert_close("O", o, ref, O_TOL)
     assert_close("LSE", lse, ref_lse, LSE_TOL)
+
+
+@pytest.mark.parametrize("q_len,n_splits", [(32, 5), (32, 16), (40, 12), (1, 16), (64, 3)])
+def test_cluster_merge_row_groups(q_len, n_splits):
+    """The cluster merge with two 16-row groups per CTA, several row groups per (batch,
+    head), a single query row and fp32 output; equal to the combine kernel's merge up to
+    fp32 rounding, and to the oracle within the stated tolerances."""
+    from bd3attn import ops
+    q, k, v = qkv(12, 2, 3, q_len, 2000)
+    args = (q.cuda(), k.cuda(), v.cuda(), 16)
+    o, lse = ops.decode_raw(*args, return_lse=True, n_splits=n_splits, out_dtype=torch.float32)
+    assert_device_ok()
+    oc, lc = ops.decode_raw(*args, return_lse=True, n_splits=n_splits + 17,
+                            out_dtype=torch.float32)  # past a cluster: the combine kernel
+    assert_device_ok()
+    ref, ref_lse = oracle.attention(q, k, v, oracle.block_causal_mask(q_len, 2000, 16))
+    assert_close("O", o, ref, O_TOL)
+    assert_close("LSE", lse, ref_lse, LSE_TOL)
+    assert_close("O cluster vs combine", o, oc, 2e-3)
+    assert_close("LSE cluster vs combine", lse, lc, 1e-4)
 
 
 @pytest.mark.parametrize("B,H,q_len,kv_len,bs", [(1, 2, 65, 65, 16), (1, 2, 200, 1000, 16),

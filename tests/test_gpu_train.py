@@ -90,6 +90,27 @@ def test_deterministic_backward(B, H, n, bs):
         assert_close("dQ det vs oracle", dq1, rdq, GRAD_TOL)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_deterministic_backward_other_dtypes(dtype):
+    """The deterministic backward with fp16 inputs and with fp32 inputs (config 1's, run on
+    fp16 operands scaled by powers of two): bitwise equal from run to run, and within the
+    stated tolerance of the oracle."""
+    B, H, n, bs = 2, 3, 256, 16
+    prev = torch.are_deterministic_algorithms_enabled()
+    torch.use_deterministic_algorithms(True)
+    try:
+        (q, k, v, do), (_, dq1, dk1, dv1) = _run(B, H, n, bs, seed=7, dtype=dtype)
+        _, (_, dq2, dk2, dv2) = _run(B, H, n, bs, seed=7, dtype=dtype)
+    finally:
+        torch.use_deterministic_algorithms(prev)
+    assert dq1.dtype == dtype
+    assert torch.equal(dq1, dq2) and torch.equal(dk1, dk2) and torch.equal(dv1, dv2)
+    rdq, rdk, rdv = oracle.attention_grads(q, k, v, do, oracle.block_diff_mask(n, bs))
+    assert_close("dQ", dq1, rdq, GRAD_TOL)
+    assert_close("dK", dk1, rdk, GRAD_TOL)
+    assert_close("dV", dv1, rdv, GRAD_TOL)
+
+
 @pytest.mark.parametrize("bs", [4, 16, 128])
 def test_against_reference_golden(golden, bs):
     """Kernel vs the outputs the reference itself produced (fp32, on bf16-valued inputs)."""
