@@ -535,12 +535,13 @@ int bd3_decode_plan(int64_t B, int64_t H, int64_t q_len, int64_t kv_len, int64_t
   const int64_t groups = (q_len + 31) / 32;
   int64_t u = pick_units_per_split(B * H * groups, tiles, sms);
   int64_t s = (tiles + u - 1) / u;
-  // a split count just above a cluster's 16 CTAs: take fewer, larger splits, merged inside
-  // the kernel, when that grid is one wave (small, launch-bound decodes)
-  if (s > kMaxClusterSplits && s <= 2 * kMaxClusterSplits) {
+  // more than a cluster's 16 splits: take 16 or fewer, larger splits merged inside the
+  // kernel instead, when that grid is one wave and a split keeps at most 32 tiles (small,
+  // launch-bound decodes, where the combine launch costs more than the longer splits)
+  if (s > kMaxClusterSplits) {
     const int64_t u2 = (tiles + kMaxClusterSplits - 1) / kMaxClusterSplits;
     const int64_t s2 = (tiles + u2 - 1) / u2;
-    if (cluster_splits(s2, B * H * groups, sms)) u = u2, s = s2;
+    if (u2 <= 32 && cluster_splits(s2, B * H * groups, sms)) u = u2, s = s2;
   }
   *n_splits = s;
   *workspace_bytes = s > 1 && !cluster_splits(s, B * H * groups, sms)
