@@ -1023,6 +1023,10 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            # this rank's step times: median and p20 / p80 (the reference harness's report)
+            "ms_step_p20_p50_p80": [round(x, 4) for x in (
+                statistics.quantiles(ms, n=10, method="inclusive")[1:8:3] if len(ms) > 1
+                else ms * 3)],
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1) from a seed",
             "config": {"workload": f"C2: BD3-LM training attention fwd+bwd, B={B}/GPU, H={H}, "
