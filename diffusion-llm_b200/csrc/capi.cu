@@ -623,9 +623,16 @@ int launch_decode(bool live, const void* q, const void* k, const void* v, void* 
     const int slot = 24 + (live ? 4 : 0) + (kmb == 1 ? 0 : 2) + (bf ? 0 : 1);
     if ((rc = set_smem(kern, bd3::DecSmem::kAlloc, slot)) != BD3_OK) return rc;
     if (n_splits > 8) {  // 9 to 16 CTAs per cluster: the non-portable sizes B200 allows
-      const cudaError_t e =
-          cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (cluster size)");
+      int dev = 0;
+      cudaError_t e = cudaGetDevice(&dev);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+      static bool done[64][8] = {};
+      const int k = slot - 24;
+      if (dev >= 64 || !done[dev][k]) {
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute (cluster size)");
+        if (dev < 64) done[dev][k] = true;
+      }
     }
     ProfScope ps(kPfDecode, stream);
     return launch_pdl_cluster(kern, grid, dim3(bd3::kDecThreads), bd3::DecSmem::kAlloc,
