@@ -199,18 +199,58 @@ def barrier(world: int):
 
 
 # ---------------------------------------------------------------------------------------
+REF_DIR = os.path.join(REPO, "baseline", "_ref")
+
+
+def reference_cpu_attention():
+    """The reference's own attention and mask, model/modules.py:738
+    (scaled_dot_product_attention) and model/bd3lm.py:10 (block_diff_mask), imported from the
+    unmodified install in baseline/_ref (which travels with the working tree); None when it
+    is not installed. The path goes after this repository's, so its `kernels` package stays
+    the one the drop-in provides."""
+    if not os.path.isdir(os.path.join(REF_DIR, "model")):
+        return None
+    if REF_DIR not in sys.path:
+        sys.path.append(REF_DIR)
+    try:
+        from model.bd3lm import block_diff_mask
+        from model.modules import scaled_dot_product_attention
+    except Exception:
+        return None
+    return scaled_dot_product_attention, block_diff_mask
+
+
 def cpu_reference_step(n: int, bs: int, heads: int, gen_seed: int = 0) -> tuple[float, float]:
     """One fwd+bwd of the reference's CPU attention (fp32, autograd) on a (1, heads, 2n, 64)
-    slice; returns (seconds, useful FLOPs of the slice)."""
-    import oracle
+    slice: the reference's own functions when baseline/_ref is installed, else the oracle's
+    restatement of them; returns (seconds, useful FLOPs of the slice)."""
     g = torch.Generator().manual_seed(gen_seed)
     q, k, v, do = (torch.randn(1, heads, 2 * n, D, generator=g) for _ in range(4))
-    mask = torch.from_numpy(oracle.block_diff_mask(n, bs))
-    t0 = time.perf_counter()
-    oracle.attention_grads(q, k, v, do, mask, dtype=torch.float32)
-    dt = time.perf_counter() - t0
+    ref = reference_cpu_attention()
+    if ref is not None:
+        sdpa, block_diff_mask = ref
+        mask = block_diff_mask(n, bs)
+        qg, kg, vg = (t.requires_grad_(True) for t in (q, k, v))
+        t0 = time.perf_counter()
+        o = sdpa(qg, kg, vg, mask)
+        torch.autograd.grad(o, (qg, kg, vg), do)
+        dt = time.perf_counter() - t0
+    else:
+        import oracle
+        mask = torch.from_numpy(oracle.block_diff_mask(n, bs))
+        t0 = time.perf_counter()
+        oracle.attention_grads(q, k, v, do, mask, dtype=torch.float32)
+        dt = time.perf_counter() - t0
     f, b = useful_flops(1, n, bs)
     return dt, (f + b) * heads / H
+
+
+def cpu_reference_kind() -> tuple[str, str]:
+    """("reference", what) when the reference's own CPU path is timed, else ("port", what)."""
+    if reference_cpu_attention() is not None:
+        return "reference", ("the reference's own model/modules.py:738 scaled_dot_product_attention "
+                             "with model/bd3lm.py:10 block_diff_mask (from baseline/_ref) + autograd")
+    return "port", "oracle restatement of model/modules.py:738-771 + autograd"
 
 
 def cpu_baseline(budget_s: float = 10.0) -> dict:
@@ -224,11 +264,11 @@ def cpu_baseline(budget_s: float = 10.0) -> dict:
         times.append(dt)
     reps = len(times)
     med = statistics.median(times)
+    kind, what = cpu_reference_kind()
     return {"value": round(flops / med / 1e12, 6), "unit": UNIT, "cores": torch.get_num_threads(),
-            "kind": "port",
+            "kind": kind,
             "sample": f"fwd+bwd of a B=1 slice (12 heads, n={N_HALF}, bs={BS}) of the workload, "
-                      f"fp32, oracle restatement of model/modules.py:738-771 + autograd, "
-                      f"median of {reps} after 1 warm-up ({med:.2f} s each)"}
+                      f"fp32, {what}, median of {reps} after 1 warm-up ({med:.2f} s each)"}
 
 
 def run_reference(args) -> None:
@@ -244,9 +284,9 @@ def run_reference(args) -> None:
         total_t += dt
         total_f += fl
     val = total_f / total_t / 1e12
+    kind, what = cpu_reference_kind()
     sample = (f"each step: fwd+bwd of a B=1 slice (12 heads, n={N_HALF}, bs={BS}) of the "
-              f"B={B} workload, fp32 on the host cores (oracle restatement of "
-              f"model/modules.py:738-771 + autograd; the reference itself cannot travel)")
+              f"B={B} workload, fp32 on the host cores ({what})")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(val, 6), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -255,7 +295,7 @@ def run_reference(args) -> None:
         "config": {"workload": f"C2 fwd+bwd B={B} H={H} n={N_HALF} bs={BS} (B=1 slice per step)",
                    "global_batch": B, "seq_len": 2 * N_HALF, "parallelism": "cpu"},
         "cpu_baseline": {"value": round(val, 6), "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(val, 6), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
