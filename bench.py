@@ -467,6 +467,37 @@ def sharded_decode_extras(dev, l2, peaks, world: int, rank: int, reps: int = 10)
             out["check"] = {"vs": "single-GPU decode of the whole cache", "o_max_abs": eo,
                             "lse_max_abs": el, "tol": 1e-3, "ok": eo <= 1e-3 and el <= 1e-3}
         barrier(world)
+        # the same step with the partials exchanged and merged over NVLink peer memory in one
+        # kernel (bd3_peer_merge) instead of the all-gather and the merge launch
+        from bd3attn.dist import PeerMerge
+        peer = PeerMerge(b, H, 16)
+
+        def step_p2p():
+            return sharded_decode(q, k_loc, v_loc, BS, a, kv, out_dtype=torch.float32, peer=peer)
+        for _ in range(3):
+            step_p2p()
+        barrier(world)
+        tp = max_over_ranks(statistics.median(time_steps(step_p2p, reps, l2)), world)
+        p2p = {"us": round(tp * 1e3, 2), "GBps": round(by / tp / 1e6, 1),
+               "frac_hbm_aggregate": round(by / tp / 1e6 / (world * peaks["hbm_gbs"]), 4)}
+        # the exchange and merge alone, beside allgather_us (the merge launch comes on top)
+        o_part, l_part = ops.decode_raw(q, k_loc, v_loc, BS, q_pos0=kv - 16, kv_pos0=a,
+                                        out_dtype=torch.float32, return_lse=True)
+        barrier(world)
+        pm = max_over_ranks(statistics.median(time_steps(
+            lambda: peer.merge(o_part, l_part, torch.float32), reps, l2)), world)
+        p2p["exchange_merge_us"] = round(pm * 1e3, 2)
+        o2, l2_ = step_p2p()
+        torch.cuda.synchronize()
+        p2p["status"] = ops.device_status(clear=True)
+        if rank == 0:
+            eo = (o2 - o_ref).abs().max().item()
+            el = (l2_ - lse_ref).abs().max().item()
+            p2p["check"] = {"vs": "single-GPU decode of the whole cache", "o_max_abs": eo,
+                            "lse_max_abs": el, "tol": 1e-3, "ok": eo <= 1e-3 and el <= 1e-3}
+        out["p2p_merge"] = p2p
+        barrier(world)
+        del peer
     return {"splitkv_b32_kv64k_seq_sharded": out}
 
 

@@ -34,6 +34,9 @@ SIGNATURES = {
                             _pi64, _i64, _i32, _vp, _sz, _vp]),
     "bd3_attn_bwd_det": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                             _pi64, _i64, _i32, _vp, _sz, _vp]),
+    "bd3_peer_merge_buffer_bytes": (_sz, [_i32, _i64, _i64, _i64]),
+    "bd3_peer_merge": (_i32, [_vp, _vp, ctypes.POINTER(ctypes.c_uint64), _i32, _i32,
+                              ctypes.c_uint64, _vp, _vp, _i64, _i64, _i64, _pi64, _i32, _vp]),
     "bd3_decode_plan": (_i32, [_i64, _i64, _i64, _i64, _i64, _i64, _i64, _pi64, _psz]),
     "bd3_decode_attn": (_i32, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _pi64,
                                _i64, _i64, _i64, _i64, _i32, _i32, _vp, _sz, _vp]),

@@ -62,17 +62,71 @@ def _gpu_merge(parts, lses, out_dtype):
     return ops.lse_merge_raw(parts, lses, out_dtype)
 
 
+class PeerMerge:
+    """The exchange buffers of sharded_decode's merge over NVLink peer memory
+    (bd3_peer_merge: every rank stores its partial straight into each peer's buffer and merges
+    what the peers stored into its own, in one kernel, instead of an NCCL all-gather and a
+    merge launch). One symmetric buffer per rank, mapped into every rank's process by torch's
+    symmetric memory and zeroed once. One instance serves one (group, B, H, rows); its epoch
+    advances by one per call, identically on every rank, since every rank calls it once per
+    step. Collective to create."""
+
+    def __init__(self, B: int, H: int, rows: int, group=None, device=None):
+        import ctypes
+
+        import torch.distributed._symmetric_memory as symm_mem
+
+        from bd3attn._lib import LIB
+        self.group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.group)
+        self.rank = dist.get_rank(self.group)
+        nbytes = LIB.bd3_peer_merge_buffer_bytes(self.world, B, H, rows)
+        if nbytes == 0:
+            raise ValueError("peer merge: 2 <= world <= 8 and sizes >= 1")
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.buf = symm_mem.empty(nbytes // 4, dtype=torch.float32, device=device)
+        self.buf.zero_()
+        torch.cuda.synchronize(device)
+        self.handle = symm_mem.rendezvous(self.buf, self.group)
+        self.ptrs = (ctypes.c_uint64 * self.world)(*self.handle.buffer_ptrs)
+        self.shape = (B, H, rows)
+        self.epoch = 0
+        dist.barrier(group=self.group)  # every buffer is zeroed before a peer stores into it
+
+    def merge(self, part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype):
+        """(O (B, H, rows, 64) in out_dtype, LSE (B, H, rows) fp32) of every rank's partial;
+        part_o (B, H, rows, 64) fp32 and part_lse (B, H, rows) fp32 are this rank's."""
+        from bd3attn import ops
+        from bd3attn._lib import LIB, check, i64_array
+        B, H, rows = self.shape
+        part_o, part_lse = part_o.float().contiguous(), part_lse.float().contiguous()
+        assert tuple(part_o.shape) == (B, H, rows, 64) and tuple(part_lse.shape) == (B, H, rows)
+        self.epoch += 1
+        o = torch.empty((B, H, rows, 64), dtype=out_dtype, device=part_o.device)
+        lse = torch.empty((B, H, rows), dtype=torch.float32, device=part_o.device)
+        with torch.cuda.device(part_o.device):
+            check("bd3_peer_merge", LIB.bd3_peer_merge(
+                ops._ptr(part_o), ops._ptr(part_lse), self.ptrs, self.world, self.rank,
+                self.epoch, ops._ptr(o), ops._ptr(lse), B, H, rows,
+                i64_array(ops._s3(o)), ops._code(out_dtype), ops._stream(part_o)))
+        return o, lse
+
+
 def sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor,
                    block_size: int, kv_start: int, kv_len_total: int,
                    group=None, out_dtype=None,
                    partial_fn: Callable = _gpu_partial,
-                   merge_fn: Callable = _gpu_merge):
+                   merge_fn: Callable = _gpu_merge,
+                   peer: "PeerMerge | None" = None):
     """Decode attention of ``q`` (B, H, q_len, 64) over a KV cache sharded by sequence.
 
     k_local/v_local: (B, H, L_r, 64), this rank's keys at global positions
     [kv_start, kv_start + L_r). The queries sit at the last q_len of kv_len_total positions
     (the reference's placement). Returns (O (B, H, q_len, 64) in out_dtype, LSE), identical
-    on every rank. A rank whose slice no query can see contributes LSE = -inf.
+    on every rank. A rank whose slice no query can see contributes LSE = -inf. With ``peer``
+    (a PeerMerge of this shape) the partials meet over NVLink peer memory in one kernel;
+    otherwise one all-gather of the process group moves them and ``merge_fn`` combines them.
     """
     world = dist.get_world_size(group)
     B, H, q_len, D = q.shape
@@ -85,6 +139,8 @@ def sharded_decode(q: torch.Tensor, k_local: torch.Tensor, v_local: torch.Tensor
     else:
         o = torch.zeros(B, H, q_len, D, dtype=torch.float32, device=q.device)
         lse = torch.full((B, H, q_len), float("-inf"), dtype=torch.float32, device=q.device)
+    if peer is not None:
+        return peer.merge(o, lse, out_dtype)
     # one all-gather of [O | LSE] per rank, packed so a single collective moves both
     packed = torch.cat([o.reshape(B, H, q_len * D), lse.reshape(B, H, q_len)], dim=-1)
     # ranks' blocks concatenated along dim 0 (the layout both NCCL and gloo produce)

@@ -17,6 +17,7 @@
 #include "decode.cuh"
 #include "f32_scale.cuh"
 #include "kv_rope.cuh"
+#include "peer_merge.cuh"
 #include "sampler.cuh"
 
 namespace {
@@ -858,6 +859,64 @@ int bd3_decode_live_blocks(const void* q, const void* k, const void* v, void* o,
                        kv_block, B, H, q_len, kv_len, strides, block_size, kv_len - q_len, 0,
                        n_splits, dtype, out_dtype, workspace, workspace_bytes,
                        static_cast<cudaStream_t>(stream));
+}
+
+size_t bd3_peer_merge_buffer_bytes(int world, int64_t B, int64_t H, int64_t rows) {
+  if (world < 2 || world > bd3::kPeerMaxWorld || B < 1 || H < 1 || rows < 1) return 0;
+  const int64_t region = (B * H * rows * 65 + 3) / 4 * 4;  // floats, 16-byte multiples
+  return static_cast<size_t>(2 * world * region) * 4 +
+         static_cast<size_t>(2 * bd3::kPeerMaxWorld * bd3::kPeerMaxCtas) * 8;
+}
+
+int bd3_peer_merge(const float* part_o, const float* part_lse, const uint64_t* peer_bufs,
+                   int world, int rank, uint64_t epoch, void* o, float* lse_out, int64_t B,
+                   int64_t H, int64_t rows, const int64_t* o_strides, int out_dtype,
+                   void* stream) {
+  if (world < 2 || world > bd3::kPeerMaxWorld || rank < 0 || rank >= world)
+    return fail(BD3_ERR_INVALID, "peer merge: 2 <= world <= %d and 0 <= rank < world",
+                bd3::kPeerMaxWorld);
+  if (B < 1 || H < 1 || rows < 1 || B * H * rows > (int64_t(1) << 30))
+    return fail(BD3_ERR_INVALID, "peer merge: sizes must be >= 1");
+  if (epoch == 0) return fail(BD3_ERR_INVALID, "peer merge: epochs start at 1");
+  if (out_dtype < BD3_BF16 || out_dtype > BD3_F32) return fail(BD3_ERR_INVALID, "bad out_dtype");
+  if (const int rc = ensure_context(); rc != BD3_OK) return rc;
+  if (reinterpret_cast<uintptr_t>(part_o) % 16 || reinterpret_cast<uintptr_t>(part_lse) % 4)
+    return fail(BD3_ERR_INVALID, "peer merge: the partial O must be 16-byte aligned");
+  const int64_t oal = out_dtype == BD3_F32 ? 4 : 8;
+  if (reinterpret_cast<uintptr_t>(o) % 16 || o_strides[0] % oal || o_strides[1] % oal ||
+      o_strides[2] % oal)
+    return fail(BD3_ERR_INVALID, "o: pointer and strides must be 16-byte aligned");
+  bd3::PeerMergeParams p{};
+  for (int r = 0; r < world; ++r) {
+    if (peer_bufs[r] == 0 || peer_bufs[r] % 16)
+      return fail(BD3_ERR_INVALID, "peer merge: exchange buffer %d missing or misaligned", r);
+    p.bufs[r] = reinterpret_cast<float*>(peer_bufs[r]);
+  }
+  int sms = 148;
+  int rc = current_device_sms(&sms);
+  if (rc != BD3_OK) return rc;
+  const int64_t units = B * H * rows;
+  int64_t ctas = units < sms ? units : sms;  // one CTA per SM at most: every CTA is resident
+  if (ctas > bd3::kPeerMaxCtas) ctas = bd3::kPeerMaxCtas;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.o = o;
+  p.lse_out = lse_out;
+  p.o_sb = o_strides[0];
+  p.o_sh = o_strides[1];
+  p.o_ss = o_strides[2];
+  p.epoch = epoch;
+  p.region = (units * 65 + 3) / 4 * 4;
+  p.world = world;
+  p.rank = rank;
+  p.H = static_cast<int>(H);
+  p.units = static_cast<int>(units);
+  p.rows = static_cast<int>(rows);
+  p.out_dtype = out_dtype;
+  ProfScope ps(kPfCombine, static_cast<cudaStream_t>(stream));
+  return launch_pdl(bd3::peer_merge_kernel, dim3(static_cast<unsigned>(ctas)),
+                    dim3(bd3::kPeerThreads), 0, static_cast<cudaStream_t>(stream),
+                    "peer_merge_kernel launch", p);
 }
 
 int bd3_lse_merge(const float* parts, const float* lses, void* o, float* lse_out, int64_t B,

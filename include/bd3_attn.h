@@ -172,6 +172,27 @@ BD3_API int bd3_decode_live_blocks(const void* q, const void* k, const void* v, 
                            int dtype, int out_dtype, void* workspace, size_t workspace_bytes,
                            void* stream);
 
+/* Exchange and merge of sequence-sharded decode in one kernel over NVLink peer memory: each
+ * rank stores its partial (O normalised over its keys, fp32; natural-log LSE) straight into
+ * every peer's exchange buffer, raises a flag there, waits (at most 1 s, then device status
+ * bit 16) for the peers' flags on its own buffer and merges the partials in rank order with
+ * the weighting of kernels/SplitKVDecodeAttention.py:109-119 (bd3_lse_merge's). It replaces
+ * the NCCL all-gather + bd3_lse_merge pair; the reference itself is single-GPU. Plain stores
+ * to peers and loads of the local buffer only (no TMA, no multicast).
+ *   part_o: (B*H*rows, 64) fp32, part_lse: (B*H*rows) fp32, this rank's partial.
+ *   peer_bufs: host array of `world` device pointers, every rank's exchange buffer as mapped
+ *   in this process (symmetric memory), bd3_peer_merge_buffer_bytes() bytes each, zeroed
+ *   once before the first call.
+ *   epoch: 1, 2, 3, ... advanced by one per call, the same on every rank.
+ *   o: (B, H, rows, 64) in out_dtype with o_strides[3]; lse_out optional (B*H, rows) fp32.
+ * Every rank must call it with the same sizes and epoch; a rank may be one call ahead of a
+ * peer, not two. */
+BD3_API size_t bd3_peer_merge_buffer_bytes(int world, int64_t B, int64_t H, int64_t rows);
+BD3_API int bd3_peer_merge(const float* part_o, const float* part_lse, const uint64_t* peer_bufs,
+                           int world, int rank, uint64_t epoch, void* o, float* lse_out,
+                           int64_t B, int64_t H, int64_t rows, const int64_t* o_strides,
+                           int out_dtype, void* stream);
+
 /* LSE-weighted merge of G partial results over disjoint key sets (the math of
  * split_kv_reduce_kern, kernels/SplitKVDecodeAttention.py:91-127; here also the merge of
  * per-GPU partials after an all-gather for sequence-sharded decode).

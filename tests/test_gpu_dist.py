@@ -1,8 +1,9 @@
 """The multi-GPU partitions on real GPUs over NCCL (needs 2 GPUs; skipped otherwise).
 
-- Sequence-sharded decode: each rank decodes its slice of the KV cache with the CUDA kernels,
-  one NCCL all-gather moves the [O | LSE] partials, and bd3_lse_merge combines them. The
-  result must equal a single-GPU decode over the whole cache.
+- Sequence-sharded decode: each rank decodes its slice of the KV cache with the CUDA kernels;
+  one NCCL all-gather moves the [O | LSE] partials and bd3_lse_merge combines them, or one
+  kernel exchanges them over NVLink peer memory and merges them (bd3_peer_merge). The result
+  must equal a single-GPU decode over the whole cache.
 - Batch x head sharding of training attention: each rank runs the forward and backward on its
   (batch, head) shard; the shards must equal the same slices of a single-GPU run.
 
@@ -54,31 +55,46 @@ def _decode_inputs(B, H, q_len, kv_len):
     return mk(q_len), mk(kv_len), mk(kv_len)
 
 
-def _decode_worker(rank, port, B, H, q_len, kv_len, bs, path):
+def _decode_worker(rank, port, B, H, q_len, kv_len, bs, path, exchange="nccl"):
     import sys
     sys.path.insert(0, os.path.join(os.path.dirname(__file__), "..", "diffusion-llm_b200"))
-    from bd3attn.dist import seq_shard, sharded_decode
+    from bd3attn.dist import PeerMerge, seq_shard, sharded_decode
     _init(rank, port)
     try:
         q, k, v = (t.cuda() for t in _decode_inputs(B, H, q_len, kv_len))
         a, b = seq_shard(kv_len, WORLD, rank)
-        o, lse = sharded_decode(q, k[:, :, a:b].contiguous(), v[:, :, a:b].contiguous(), bs, a,
-                                kv_len, out_dtype=torch.float32)
+        kl, vl = k[:, :, a:b].contiguous(), v[:, :, a:b].contiguous()
+        peer = PeerMerge(B, H, q_len) if exchange == "p2p" else None
+        results = []
+        # several calls in a row: the exchange alternates buffer parities by epoch
+        for _ in range(3 if peer is not None else 1):
+            o, lse = sharded_decode(q, kl, vl, bs, a, kv_len, out_dtype=torch.float32,
+                                    peer=peer)
+            results.append((o.clone(), lse.clone()))
         torch.cuda.synchronize()
+        from bd3attn import ops
+        assert ops.device_status(clear=True) == 0
+        for o2, l2 in results[1:]:  # every call gives the first one's result, bit for bit
+            assert torch.equal(o2, results[0][0]) and torch.equal(l2, results[0][1])
         if rank == 0:
-            torch.save((o.cpu(), lse.cpu()), path)
+            torch.save((results[0][0].cpu(), results[0][1].cpu()), path)
         dist.barrier()
+        del peer
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "p2p"])
 @pytest.mark.parametrize("B,H,q_len,kv_len,bs", [(2, 12, 16, 4160, 16), (1, 4, 40, 1000, 8)])
-def test_sharded_decode_nccl_equals_single_gpu(tmp_path, B, H, q_len, kv_len, bs):
+def test_sharded_decode_equals_single_gpu(tmp_path, B, H, q_len, kv_len, bs, exchange):
+    """The partials meet through an NCCL all-gather and bd3_lse_merge, or through NVLink peer
+    memory in one kernel (bd3_peer_merge, three calls in a row, equal to each other bit for
+    bit); either way the merged result equals a single-GPU decode of the whole cache."""
     _need_gpus()
     from bd3attn import ops
     path = str(tmp_path / "out.pt")
-    mp.spawn(_decode_worker, args=(_free_port(), B, H, q_len, kv_len, bs, path), nprocs=WORLD,
-             join=True)
+    mp.spawn(_decode_worker, args=(_free_port(), B, H, q_len, kv_len, bs, path, exchange),
+             nprocs=WORLD, join=True)
     o, lse = torch.load(path)
     q, k, v = (t.cuda() for t in _decode_inputs(B, H, q_len, kv_len))
     ref_o, ref_lse = ops.decode_raw(q, k, v, bs, out_dtype=torch.float32, return_lse=True)
