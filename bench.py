@@ -885,9 +885,8 @@ def reference_extras() -> dict:
 def run_ours(args) -> None:
     world, rank, local = dist_setup(args.gpus)
     # the whole process (and the threads it starts: autograd's device thread, the clock
-    # sampler) on the GPU's NUMA-local cores: the e2e loop is paced by the host's launches
-    # between copies, and on a shared machine a thread that wanders onto a busy core made
-    # its steps up to 5x slower
+    # sampler) on the GPU's NUMA-local cores, where the pinned host buffers of the e2e
+    # copies are allocated
     local_cpus = gpu_local_cpus(local)
     if local_cpus:
         os.sched_setaffinity(0, local_cpus)
