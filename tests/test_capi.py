@@ -112,3 +112,38 @@ def test_wait_self_check_rejects_bad_limits_on_the_host():
     assert LIB.bd3_debug_wait_timeout(2 * 10 ** 9, 0, None, None) == BD3_ERR_INVALID
     assert b"limit_ns" in LIB.bd3_last_error()
     assert LIB.bd3_debug_wait_timeout(10 ** 6, 0, None, None) == BD3_ERR_INVALID  # no buffer
+
+
+def _peer_merge(**over):
+    """bd3_peer_merge with the given arguments changed; every pointer is a dummy, so only
+    calls that fail its host-side checks (made before any CUDA call) may be made here."""
+    import ctypes
+    from bd3attn._lib import LIB, i64_array
+    a = dict(world=2, rank=0, epoch=1, B=1, H=2, rows=16, out_dtype=0)
+    a.update(over)
+    bufs = (ctypes.c_uint64 * 8)(*([0x10000] * 8))
+    return LIB.bd3_peer_merge(0x1000, 0x2000, bufs, a["world"], a["rank"], a["epoch"], 0x3000,
+                              None, a["B"], a["H"], a["rows"], i64_array([0] * 3),
+                              a["out_dtype"], None)
+
+
+def test_peer_merge_buffer_size_and_argument_checks():
+    """The exchange buffer of the peer-memory merge holds, per parity and sender, every
+    (batch, head, row)'s 64 O values and its LSE (rounded up to 16 bytes), then the per-chunk
+    flags; sizes and ranks outside the supported range are refused before the GPU is used."""
+    from bd3attn._lib import BD3_ERR_INVALID, LIB
+    for world, B, H, rows in ((2, 1, 2, 16), (4, 32, 12, 16), (8, 3, 5, 7)):
+        region = (B * H * rows * 65 + 3) // 4 * 4
+        assert LIB.bd3_peer_merge_buffer_bytes(world, B, H, rows) == \
+            2 * world * region * 4 + 2 * 8 * 256 * 8
+    for bad in ((1, 1, 2, 16), (9, 1, 2, 16), (2, 0, 2, 16), (2, 1, 2, 0)):
+        assert LIB.bd3_peer_merge_buffer_bytes(*bad) == 0
+    assert _peer_merge(world=1) == BD3_ERR_INVALID
+    assert b"world" in LIB.bd3_last_error()
+    assert _peer_merge(world=9) == BD3_ERR_INVALID
+    assert _peer_merge(rank=2) == BD3_ERR_INVALID
+    assert _peer_merge(rank=-1) == BD3_ERR_INVALID
+    assert _peer_merge(B=0) == BD3_ERR_INVALID
+    assert _peer_merge(epoch=0) == BD3_ERR_INVALID
+    assert b"epoch" in LIB.bd3_last_error()
+    assert _peer_merge(out_dtype=5) == BD3_ERR_INVALID
