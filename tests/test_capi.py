@@ -147,3 +147,17 @@ def test_peer_merge_buffer_size_and_argument_checks():
     assert _peer_merge(epoch=0) == BD3_ERR_INVALID
     assert b"epoch" in LIB.bd3_last_error()
     assert _peer_merge(out_dtype=5) == BD3_ERR_INVALID
+
+
+def test_backward_workspace_sizes():
+    """The backward's workspace: per query row Delta and LSE*log2(e) (fp32), then the dQ
+    accumulator: 64 fp32 values, or 64 int64 fixed-point values for the deterministic
+    variant. Non-positive sizes give 0."""
+    from bd3attn._lib import LIB
+    for B, H, n in ((1, 1, 128), (8, 12, 1024), (2, 3, 256)):
+        rows = B * H * 2 * n
+        assert LIB.bd3_attn_bwd_workspace_size(B, H, n, 64) == rows * (2 + 64) * 4
+        assert LIB.bd3_attn_bwd_det_workspace_size(B, H, n, 64) == rows * (2 * 4 + 64 * 8)
+    for bad in ((0, 1, 128), (1, 0, 128), (1, 1, 0)):
+        assert LIB.bd3_attn_bwd_workspace_size(*bad, 64) == 0
+        assert LIB.bd3_attn_bwd_det_workspace_size(*bad, 64) == 0
